@@ -1,0 +1,660 @@
+#!/usr/bin/env python
+"""Expert-cache hot-path benchmark on B200: miss-gather GB/s against the host link.
+
+Workload (one MoE layer, Qwen3-30B-A3B W8A8 shapes, TP1): 128 experts of 4,732,928 B
+(w13 int8 [1536,2048], w2 int8 [2048,768], fp32 per-row scales) in pinned host memory,
+S device slots, a decode step of ``tokens`` x top-8 routing ids carrying exactly
+``misses`` experts that are not resident.  One step = one ``expert_cache_manage_remap``
+launch (policy + victim choice + remap) followed by one ``expert_cache_gather`` launch
+(the missing slabs over the host link into their slots).
+
+Forced misses are planned with the product kernel itself in an untimed pass (host reads
+of the table choose ``misses`` absent and ``8*tokens - misses`` resident experts per
+step); the timed passes replay that trace from the same initial state, and the kernel's
+determinism makes every replay install exactly the planned experts (checked).
+
+Printed (rank 0, one JSON line): ``value`` = gathered bytes / device time of the K timed
+steps with inputs resident (max over ranks, summed over ranks); ``e2e`` = the same bytes
+through ``ExpertSlotCache.refresh`` with the routing ids copied in from pinned host
+memory and the slot ids copied back every step; ``roofline`` for the gather kernel
+against the pinned host-to-device copy-engine bandwidth measured in the same run;
+``cpu_baseline`` = the CPU oracle (policy step + memcpy of the slabs) on one host core.
+
+``--impl reference`` runs the CPU restatement of the reference's policy path on all
+usable host cores (policy step + host memcpy of the same slabs into host slot buffers),
+rank 0 only.  ``--sweep`` prints one line per (slots, misses, tokens) point of the
+single-layer microbenchmark grid.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "vllm-expert-cache_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "miss-gather GB/s vs host-link peak"
+E_EXPERTS = 128
+TOP_K = 8
+L2_BYTES = 126 * 1024 * 1024
+# dram__bytes_read.sum + dram__bytes_write.sum of one gather launch at this workload
+# (4 misses), from the ncu capture summarised in profiles/gather_kernel_s64_m4.txt
+GATHER_DRAM_BYTES = None
+
+
+def parse(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--slots", type=int, default=64)
+    ap.add_argument("--misses", type=int, default=4)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--policy", choices=["lfu", "lru"], default="lfu")
+    ap.add_argument("--decay", type=int, default=64)
+    ap.add_argument("--chunks", type=int, default=None)
+    ap.add_argument("--lanes", type=int, default=None)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args(argv)
+    if a.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return a
+
+
+# ---------------------------------------------------------------------------------------
+# distributed plumbing (replicas: no collective on the data path)
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+
+    def init(self, backend="nccl"):
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=180))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            import torch
+            if dist.get_backend() == "nccl":
+                dist.barrier(device_ids=[torch.cuda.current_device()])
+            else:
+                dist.barrier()
+
+    def max(self, x: float, device=None) -> float:
+        return self._reduce(x, "max", device)
+
+    def sum(self, x: float, device=None) -> float:
+        return self._reduce(x, "sum", device)
+
+    def _reduce(self, x, op, device):
+        if not self.pg:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------
+# clocks during the timed region (NVML)
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period=0.05):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            prop = torch.cuda.get_device_properties(device_index)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report it rather than invent clocks
+            self.h = None
+            self.err = repr(e)
+        self.period = period
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                util = nv.nvmlDeviceGetUtilizationRates(self.h).gpu
+                self.samples.append((mhz, r, util))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.h is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        busy = [s for s in self.samples if s[2] > 0] or self.samples
+        bits = 0
+        for _, r, _ in busy:
+            bits |= r
+        names = [n for b, n in _REASONS.items() if bits & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median([s[0] for s in busy]) if busy else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(busy)}
+
+
+# ---------------------------------------------------------------------------------------
+# workload
+
+def h2d_peak_gbs(device, nbytes=512 << 20, reps=10):
+    """Pinned host -> device copy-engine bandwidth (the host-link denominator)."""
+    import torch
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    src.fill_(1)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    best = 0.0
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        b.synchronize()
+        best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del src, dst
+    return best
+
+
+class Layer:
+    """One layer's host experts, device slots and cache state (C-ABI level)."""
+
+    def __init__(self, S, seed, device, policy_code, decay, chunks, lanes):
+        import torch
+        from vllm_expert_cache import synthetic
+        self.torch = torch
+        self.device = device
+        self.E, self.S = E_EXPERTS, S
+        self.policy, self.decay = policy_code, decay
+        self.chunks, self.lanes = chunks, lanes
+        self.host = synthetic.qwen3_30b_a3b_experts(E=self.E, seed=seed)
+        self.names = list(self.host)
+        self.sizes = [synthetic.bytes_per_expert(self.host[n]) for n in self.names]
+        self.src = [synthetic.host_device_pointer(self.host[n]) for n in self.names]
+        self.slots = [torch.empty((S,) + tuple(self.host[n].shape[1:]),
+                                  dtype=self.host[n].dtype, device=device)
+                      for n in self.names]
+        self.bytes_per_expert = sum(self.sizes)
+        rng = __import__("numpy").random.default_rng(seed + 1000)
+        self.hot = sorted(rng.choice(self.E, size=S, replace=False).tolist())
+        i32, i64 = torch.int32, torch.int64
+        self.state = {
+            "table": torch.full((self.E,), -1, dtype=i32, device=device),
+            "map_cold": torch.arange(self.E, dtype=i32, device=device),
+            "slot_expert": torch.full((S,), -1, dtype=i32, device=device),
+            "slot_stamp": torch.zeros((S,), dtype=i64, device=device),
+            "routed": torch.zeros((self.E,), dtype=torch.uint8, device=device),
+            "step": torch.zeros((1,), dtype=i64, device=device),
+            "miss": torch.zeros((2 * S,), dtype=i32, device=device),
+            "n_miss": torch.zeros((1,), dtype=i32, device=device),
+        }
+        self.reset()
+        from vllm_expert_cache import _lib
+        self.h = _lib.lib()
+        P = ctypes.c_void_p
+        st = self.state
+        self._sp = [P(st[k].data_ptr()) for k in ("table", "map_cold", "slot_expert",
+                                                   "slot_stamp", "routed", "step", "miss",
+                                                   "n_miss")]
+        trip = []
+        for d, s, b in zip(self.slots, self.src, self.sizes):
+            trip += [P(d.data_ptr()), P(s), ctypes.c_long(b)]
+        while len(trip) < 18:
+            trip += trip[-3:]
+        self._gather_args = trip + [P(st["miss"].data_ptr()), P(st["n_miss"].data_ptr()),
+                                    chunks, lanes]
+
+    def reset(self):
+        torch = self.torch
+        st = self.state
+        hot = torch.tensor(self.hot, dtype=torch.int64, device=self.device)
+        st["table"].fill_(-1)
+        st["table"][hot] = torch.arange(self.S, dtype=torch.int32, device=self.device)
+        st["map_cold"].copy_(torch.arange(self.E, dtype=torch.int32, device=self.device))
+        st["map_cold"][hot] = -1
+        st["slot_expert"].copy_(hot.to(torch.int32))
+        st["slot_stamp"].zero_()
+        st["routed"].zero_()
+        st["step"].zero_()
+        st["miss"].zero_()
+        st["n_miss"].zero_()
+
+    def snapshot(self):
+        return {k: v.cpu().clone() for k, v in self.state.items()
+                if k in ("table", "map_cold", "slot_expert", "slot_stamp", "step")}
+
+    def manage(self, ids, out, stream):
+        mk = ids.numel()
+        rc = self.h.expert_cache_manage_remap(
+            ctypes.c_void_p(ids.data_ptr()), mk, self.E, self.S, min(self.E, mk), self.S,
+            *self._sp, self.policy, self.decay, ctypes.c_void_p(out.data_ptr()), 4, stream)
+        if rc:
+            raise RuntimeError(f"expert_cache_manage_remap rc={rc}")
+
+    def gather(self, stream):
+        rc = self.h.expert_cache_gather(*self._gather_args, stream)
+        if rc:
+            raise RuntimeError(f"expert_cache_gather rc={rc}")
+
+
+def plan_trace(layer: Layer, steps, misses, tokens, seed):
+    """Routing ids with exactly ``misses`` non-resident experts per step, chosen from the
+    state the product kernel reaches (host reads between steps; untimed)."""
+    import numpy as np
+    import torch
+    D = TOP_K * tokens
+    if D > layer.S or misses > D:
+        raise ValueError(f"{tokens} tokens x top-{TOP_K} do not fit {layer.S} slots")
+    rng = np.random.default_rng(seed + 7)
+    mk = D
+    trace = np.empty((steps, mk), dtype=np.int32)
+    out = torch.empty(mk, dtype=torch.int32, device=layer.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    layer.reset()
+    for t in range(steps):
+        table = layer.state["table"].cpu().numpy()
+        absent = np.flatnonzero(table < 0)
+        resident = np.flatnonzero(table >= 0)
+        chosen = np.concatenate([rng.choice(absent, misses, replace=False),
+                                 rng.choice(resident, D - misses, replace=False)])
+        rng.shuffle(chosen)
+        rows = [chosen[(r * TOP_K + np.arange(TOP_K)) % D] for r in range(tokens)]
+        trace[t] = np.concatenate(rows)
+        layer.manage(torch.from_numpy(trace[t]).to(layer.device), out, stream)
+    torch.cuda.synchronize()
+    final = layer.snapshot()
+    layer.reset()
+    return trace, final
+
+
+def check_replay(layer: Layer, final, what):
+    for k, v in layer.snapshot().items():
+        if not layer.torch.equal(v, final[k]):
+            raise RuntimeError(f"{what}: replay diverged from the planned trace ({k})")
+
+
+def value_pass(layer, trace_dev, out_dev, W, K, dist):
+    import torch
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    layer.reset()
+    for t in range(W):
+        layer.manage(trace_dev[t], out_dev[t], stream)
+        layer.gather(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for t in range(W, W + K):
+        layer.manage(trace_dev[t], out_dev[t], stream)
+        layer.gather(stream)
+    b.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+def kernel_pass(layer, trace_dev, out_dev, W, K):
+    """Per-launch device time of each kernel (events around every launch)."""
+    import torch
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    layer.reset()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    for t in range(W):
+        layer.manage(trace_dev[t], out_dev[t], stream)
+        layer.gather(stream)
+    for i, t in enumerate(range(W, W + K)):
+        ev[i][0].record()
+        layer.manage(trace_dev[t], out_dev[t], stream)
+        ev[i][1].record()
+        layer.gather(stream)
+        ev[i][2].record()
+    torch.cuda.synchronize()
+    man = [e[0].elapsed_time(e[1]) * 1e3 for e in ev]
+    gat = [e[1].elapsed_time(e[2]) * 1e3 for e in ev]
+    floor = []
+    for _ in range(200):
+        x, y = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x.record()
+        torch.cuda._sleep(0)
+        y.record()
+        floor.append((x, y))
+    torch.cuda.synchronize()
+    fl = [x.elapsed_time(y) * 1e3 for x, y in floor]
+    return statistics.mean(man), statistics.mean(gat), statistics.median(fl)
+
+
+def e2e_pass(layer, trace, W, K, tokens):
+    """Through the public per-layer API (ExpertSlotCache.refresh) with host buffers."""
+    import torch
+    from vllm_expert_cache import synthetic
+    from vllm_expert_cache.cache import ExpertSlotCache
+
+    class Owner(torch.nn.Module):
+        pass
+
+    owner = Owner()
+    views = {n: synthetic.uva_view(layer.host[n], layer.device) for n in layer.names}
+    for n, v in views.items():
+        owner.register_parameter(n, torch.nn.Parameter(v, requires_grad=False))
+    cache = ExpertSlotCache(owner, layer.names, layer.E, layer.S, layer.device,
+                            required=set(layer.names[:2]))
+    cache.policy, cache.decay = layer.policy, layer.decay
+    cache.chunks, cache.lanes = layer.chunks, layer.lanes
+    # same initial state as the C-ABI passes
+    layer.reset()
+    for k in ("table", "map_cold", "slot_expert", "slot_stamp", "routed", "step", "miss",
+              "n_miss"):
+        getattr(cache, k).copy_(layer.state[k])
+    mk = trace.shape[1]
+    h_ids = torch.from_numpy(trace).pin_memory()
+    h_out = torch.empty_like(h_ids).pin_memory()
+    for t in range(W):
+        ids = h_ids[t].to(layer.device, non_blocking=True).view(tokens, TOP_K)
+        h_out[t].copy_(cache.refresh(ids).view(-1), non_blocking=True)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for t in range(W, W + K):
+        ids = h_ids[t].to(layer.device, non_blocking=True).view(tokens, TOP_K)
+        h_out[t].copy_(cache.refresh(ids).view(-1), non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    return ms, h_out, mk * 4, mk * 4, cache
+
+
+def cpu_baseline_port(layer, trace, steps):
+    """The CPU oracle on one host core: C policy step + memcpy of the installed slabs."""
+    import numpy as np
+    from oracle import policy, policy_c
+    st = policy.CacheState.warm(layer.E, layer.S, layer.hot)
+    hosts = [layer.host[n].view(layer.torch.uint8).reshape(-1).numpy() for n in layer.names]
+    dsts = [np.empty(layer.S * b, dtype=np.uint8) for b in layer.sizes]
+    for d in dsts:
+        d.fill(0)
+    moved = 0
+    t0 = time.perf_counter()
+    for t in range(steps):
+        policy_c.manage(st, trace[t], min(layer.E, trace.shape[1]), layer.S, layer.policy,
+                        layer.decay)
+        policy_c.gather(dsts, hosts, layer.sizes, st.miss, st.n_miss)
+        moved += int(st.n_miss[0]) * layer.bytes_per_expert
+    dt = time.perf_counter() - t0
+    return moved / dt / 1e9, dt
+
+
+# ---------------------------------------------------------------------------------------
+
+def run_ours(a, dist):
+    import numpy as np
+    import torch
+    from vllm_expert_cache.config import settings
+    dist.init("nccl")
+    dev = torch.device("cuda", dist.local if dist.world > 1 else 0)
+    torch.cuda.set_device(dev)
+    sys.path.insert(0, str(ROOT / "vllm-expert-cache_b200"))
+    import build_lib
+    if not build_lib.OUT.exists():
+        raise FileNotFoundError(f"{build_lib.OUT} missing: run __graft_entry__.build()")
+    chunks = a.chunks or settings.chunks
+    lanes = a.lanes or settings.lanes
+    policy_code = 1 if a.policy == "lfu" else 0
+    points = [(a.slots, a.misses, a.tokens)]
+    if a.sweep:
+        points = [(S, m, T) for T in (1, 4) for S in (16, 32, 64, 96) for m in (1, 2, 4, 8)
+                  if TOP_K * T <= S]
+    peak = h2d_peak_gbs(dev)
+    layer = None
+    for S, m, T in points:
+        if layer is None or layer.S != S:
+            layer = Layer(S, a.seed + dist.rank, dev, policy_code, a.decay, chunks, lanes)
+        W, K = a.warmup, a.steps
+        trace, final = plan_trace(layer, W + K, m, T, a.seed)
+        trace_dev = torch.from_numpy(trace).to(dev)
+        out_dev = torch.empty_like(trace_dev)
+        with ClockSampler(dev.index) as clk:
+            ms = value_pass(layer, trace_dev, out_dev, W, K, dist)
+        check_replay(layer, final, "value pass")
+        ms_max = dist.max(ms, dev)
+        bytes_step = m * layer.bytes_per_expert
+        total_bytes = dist.sum(float(K * bytes_step), dev)
+        value = total_bytes / (ms_max * 1e-3) / 1e9
+        man_us, gat_us, floor_us = kernel_pass(layer, trace_dev, out_dev, W, K)
+        check_replay(layer, final, "kernel pass")
+        achieved = bytes_step / (gat_us * 1e-6) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": dist.world, "steps": K, "warmup": W,
+            "ms_per_step": round(ms_max / K, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {
+                "workload": "single-layer gather/manage microbench (Qwen3-30B-A3B W8A8 "
+                            "expert slabs, TP1)",
+                "experts": E_EXPERTS, "slots": S, "misses_per_step": m,
+                "tokens_per_step": T, "top_k": TOP_K,
+                "bytes_per_expert": layer.bytes_per_expert, "policy": a.policy,
+                "decay": a.decay, "gather_ctas": chunks * lanes,
+                "l2": f"inputs larger than L2: {E_EXPERTS * layer.bytes_per_expert >> 20} "
+                      f"MiB host experts, {S * layer.bytes_per_expert >> 20} MiB slots "
+                      f"(L2 {L2_BYTES >> 20} MiB)",
+                "parallelism": f"replicas x{dist.world} (no collective on the cache path)"},
+            "host_link_peak_gbs": round(peak, 3),
+            "host_link_frac": round(value / dist.world / peak, 4),
+            "manage_us_per_layer": round(man_us, 3),
+            "gather_us_per_launch": round(gat_us, 3),
+            "empty_kernel_us": round(floor_us, 3),
+            "roofline": {"bound": "host-link", "achieved": round(achieved, 3),
+                         "peak": round(peak, 3), "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "traffic": GATHER_DRAM_BYTES if (S, m, T) == (64, 4, 1) else None,
+                         "peak_source": "pinned cudaMemcpyAsync H2D, measured in this run"},
+            "gpu_launches": 2 * K,
+            "clocks": clk.summary(),
+        }
+        if not a.sweep and not a.no_e2e:
+            ms_e, h_out, hb, db, _ = e2e_pass(layer, trace, W, K, T)
+            if not torch.equal(h_out[W:], out_dev[W:].cpu()):
+                raise RuntimeError("e2e pass: slot ids differ from the C-ABI pass")
+            ms_e = dist.max(ms_e, dev)
+            line["e2e"] = {"value": round(total_bytes / (ms_e * 1e-3) / 1e9, 3),
+                           "unit": "GB/s", "h2d_bytes_per_step": hb,
+                           "d2h_bytes_per_step": db,
+                           "api": "ExpertSlotCache.refresh (pinned ids in, slot ids out)"}
+        if not a.sweep and not a.no_cpu and dist.rank == 0 and dist.world == 1:
+            n = min(K, 200)
+            gbs, dt = cpu_baseline_port(layer, trace[W:], n)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"{n} steps of the same trace: C restatement of the policy step "
+                          f"+ memcpy of the installed slabs host->host ({dt:.2f} s)"}
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+        del trace_dev, out_dev
+    dist.barrier()
+    dist.close()
+
+
+# ---------------------------------------------------------------------------------------
+# reference arm: the CPU restatement of the reference's policy path, all host cores
+
+def _ref_worker(args):
+    shm_name, shapes, sizes, S, hot, trace, policy_code, decay, steps, warm = args
+    import numpy as np
+    from multiprocessing import shared_memory
+    from oracle import policy, policy_c
+    shm = shared_memory.SharedMemory(name=shm_name)
+    try:
+        base = np.ndarray((sum(shapes),), dtype=np.uint8, buffer=shm.buf)
+        hosts, off = [], 0
+        for n in shapes:
+            hosts.append(base[off:off + n])
+            off += n
+        dsts = [np.zeros(S * b, dtype=np.uint8) for b in sizes]
+        st = policy.CacheState.warm(E_EXPERTS, S, hot)
+        mk = trace.shape[1]
+        for t in range(warm):
+            policy_c.manage(st, trace[t], min(E_EXPERTS, mk), S, policy_code, decay)
+            policy_c.gather(dsts, hosts, sizes, st.miss, st.n_miss)
+        moved = 0
+        t0 = time.perf_counter()
+        for t in range(warm, warm + steps):
+            policy_c.manage(st, trace[t], min(E_EXPERTS, mk), S, policy_code, decay)
+            policy_c.gather(dsts, hosts, sizes, st.miss, st.n_miss)
+            moved += int(st.n_miss[0]) * sum(sizes)
+        dt = time.perf_counter() - t0
+        del base, hosts
+        return moved, t0, t0 + dt
+    finally:
+        shm.close()
+
+
+def run_reference(a, dist):
+    import multiprocessing as mp
+    from multiprocessing import shared_memory
+
+    import numpy as np
+    from oracle import policy, policy_c
+    if dist.rank != 0:
+        return
+    S, m, T = a.slots, a.misses, a.tokens
+    policy_code = 1 if a.policy == "lfu" else 0
+    i = 768
+    shapes_pe = [2 * i * 2048, 2048 * i, 2 * i * 4, 2048 * 4]    # bytes per expert
+    E = E_EXPERTS
+    total = E * sum(shapes_pe)
+    shm = shared_memory.SharedMemory(create=True, size=total)
+    try:
+        rng = np.random.default_rng(a.seed)
+        buf = np.ndarray((total,), dtype=np.uint8, buffer=shm.buf)
+        buf[:] = rng.integers(0, 256, size=total, dtype=np.uint8)
+        del buf
+        hot = sorted(np.random.default_rng(a.seed + 1000).choice(E, S, replace=False).tolist())
+        # plan the forced-miss trace with the oracle (untimed)
+        D = TOP_K * T
+        st = policy.CacheState.warm(E, S, hot)
+        W, K = a.warmup, a.steps
+        trace = np.empty((W + K, D), dtype=np.int32)
+        prng = np.random.default_rng(a.seed + 7)
+        for t in range(W + K):
+            absent, resident = np.flatnonzero(st.table < 0), np.flatnonzero(st.table >= 0)
+            ch = np.concatenate([prng.choice(absent, m, replace=False),
+                                 prng.choice(resident, D - m, replace=False)])
+            prng.shuffle(ch)
+            trace[t] = np.concatenate([ch[(r * TOP_K + np.arange(TOP_K)) % D]
+                                       for r in range(T)])
+            policy_c.manage(st, trace[t], min(E, D), S, policy_code, a.decay)
+        cores = len(os.sched_getaffinity(0))
+        try:
+            import psutil
+            avail = psutil.virtual_memory().available
+        except Exception:
+            avail = 64 << 30
+        per_worker = S * sum(shapes_pe)
+        workers = max(1, min(cores, int(avail * 0.3 // per_worker)))
+        sizes = list(shapes_pe)
+        shapes = [E * b for b in shapes_pe]
+        job = (shm.name, shapes, sizes, S, hot, trace, policy_code, a.decay, K, W)
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(workers) as pool:
+            res = pool.map(_ref_worker, [job] * workers)
+        moved = sum(r[0] for r in res)
+        span = max(r[2] for r in res) - min(r[1] for r in res)
+        gbs = moved / span / 1e9
+        line = {
+            "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+            "n_gpus": dist.world, "steps": K, "warmup": W,
+            "ms_per_step": round(span * 1e3 / K, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": "single-layer gather/manage microbench (Qwen3-30B-A3B "
+                                   "W8A8 expert slabs, TP1)",
+                       "experts": E, "slots": S, "misses_per_step": m, "tokens_per_step": T,
+                       "top_k": TOP_K, "bytes_per_expert": sum(shapes_pe),
+                       "policy": a.policy, "decay": a.decay,
+                       "parallelism": f"{workers} independent CPU replicas"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": workers,
+                             "kind": "port",
+                             "sample": f"{workers} processes x {K} steps: C restatement of "
+                                       "the reference policy step + memcpy of the installed "
+                                       "slabs host->host (the reference has no CPU gather)"},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+    finally:
+        shm.close()
+        shm.unlink()
+
+
+def main(argv=None):
+    a = parse(argv)
+    dist = Dist()
+    if dist.world == 1 and a.gpus > 1:
+        raise SystemExit("--gpus N > 1 runs under torchrun (one process per GPU)")
+    if a.impl == "reference":
+        run_reference(a, dist)
+    else:
+        run_ours(a, dist)
+
+
+if __name__ == "__main__":
+    main()

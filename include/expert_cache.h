@@ -1,0 +1,100 @@
+/* libexpertcache.so -- C-ABI of the B200 (sm_100a) expert cache.
+ *
+ * Drop-in for the reference's libexpertcache.so: the same symbol names, argument order,
+ * argument meaning and return codes, with cudaStream_t in place of hipStream_t.  Every
+ * pointer is device-accessible memory owned by the caller (PyTorch tensors passed as raw
+ * pointers; gather sources may be UVA views of pinned host memory).  Every call only
+ * enqueues work on `stream`: no host synchronisation, no allocation, no library state
+ * beyond per-device kernel attributes, so every call is legal inside CUDA-graph capture.
+ *
+ * Return codes: 0 = enqueued; -1 = arguments refused (nothing enqueued); any other value
+ * is the cudaError_t of the launch.
+ */
+#ifndef EXPERT_CACHE_H
+#define EXPERT_CACHE_H
+
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define EXPERT_CACHE_API __attribute__((visibility("default")))
+#else
+#define EXPERT_CACHE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Largest slot count / insert cap per call (reference kernels/expert_cache.hip:80-81). */
+#define EXPERT_CACHE_MAX_SLOTS 1024
+#define EXPERT_CACHE_MAX_INSERTS 1024
+/* Largest expert count.  The reference manage kernel has no bound; this one mirrors the
+ * expert->slot table in shared memory, which bounds E (E * 5 bytes + slot state). */
+#define EXPERT_CACHE_MAX_EXPERTS 32768
+/* Number of (dst, src, bytes) triples one gather call takes (reference _lib.py:61). */
+#define EXPERT_CACHE_GATHER_SLOTS 6
+
+/* One policy step for one MoE layer: mark the routed experts, refresh hit priorities
+ * (LRU: stamp = step; LFU: stamp + 1, halved every `decay` steps), evict the lowest
+ * (stamp, slot) slots whose expert is not routed this step, rewrite table / map_cold /
+ * slot_expert / slot_stamp, and emit the (expert, slot) miss list in ascending expert id.
+ *
+ *   topk_ids     [mk] int32 routed expert ids; < 0 is padding, >= E is ignored
+ *   max_distinct more distinct routed experts than this: read-through (only `step` and
+ *                `routed` change)
+ *   max_inserts  cap on installs this call; `miss` must hold 2*max_inserts ints
+ *   table        [E] expert -> slot or -1          map_cold [E] expert -> itself or -1
+ *   slot_expert  [S] slot -> expert or -1          slot_stamp [S] int64 priority
+ *   routed       [E] uint8 scratch: left holding this step's routed flags
+ *   step         [1] int64 call counter            miss [2*max_inserts], n_miss [1]
+ *   policy       0 = LRU, 1 = LFU                  decay  LFU halving period, 0 = never
+ *
+ * Returns -1 if E <= 0, E > EXPERT_CACHE_MAX_EXPERTS, S <= 0, S > EXPERT_CACHE_MAX_SLOTS,
+ * max_inserts outside [0, EXPERT_CACHE_MAX_INSERTS] or policy outside {0, 1}; mk <= 0 is
+ * an empty step (the counter still advances).
+ *
+ * Replaces: expert_cache_manage, reference kernels/expert_cache.hip:592-603 (kernel
+ * :191-282), bound by vllm_expert_cache/_lib.py:44-47, called from cache.py:118-133. */
+EXPERT_CACHE_API int expert_cache_manage(const int* topk_ids, int mk, int E, int S, int max_distinct,
+                        int max_inserts, int* table, int* map_cold, int* slot_expert,
+                        long long* slot_stamp, unsigned char* routed, long long* step,
+                        int* miss, int* n_miss, int policy, int decay,
+                        cudaStream_t stream);
+
+/* expert_cache_manage followed, in the same single-CTA launch, by the routing remap
+ * out_ids[i] = table[topk_ids[i]] on the updated table (torch indexing semantics: a
+ * negative id counts from the end; ids outside [-E, E) give -1).  out_ids holds mk
+ * elements of out_elem_bytes (4 = int32, 8 = int64) each.  Returns -1 on the manage
+ * rules above or when out_ids is NULL / out_elem_bytes is not 4 or 8.
+ *
+ * Replaces: the torch remap `table[topk_ids.to(int64)].to(topk_ids.dtype)` of reference
+ * vllm_expert_cache/cache.py:108-110 that follows the manage call at :118-163.  It has
+ * no counterpart symbol in the reference library. */
+EXPERT_CACHE_API int expert_cache_manage_remap(const int* topk_ids, int mk, int E, int S, int max_distinct,
+                              int max_inserts, int* table, int* map_cold, int* slot_expert,
+                              long long* slot_stamp, unsigned char* routed, long long* step,
+                              int* miss, int* n_miss, int policy, int decay, void* out_ids,
+                              int out_elem_bytes, cudaStream_t stream);
+
+/* Copy every installed miss's slabs: for j < *n_miss, e = miss[2j], s = miss[2j+1],
+ * dst_k[s*b_k .. (s+1)*b_k) = src_k[e*b_k .. (e+1)*b_k) for the six triples.  Sources are
+ * usually UVA views of pinned host memory (the copy then streams over the host link).
+ * Identical triples (the caller's padding) are copied once.  chunks * lanes is the CTA
+ * budget of the launch (defaults 16 * 64 in the reference's Python layer).
+ *
+ * Returns -1 if any b_k <= 0 or b_k % 16, any dst/src not 16-byte aligned, or
+ * chunks <= 0 / lanes <= 0.
+ *
+ * Replaces: expert_cache_gather, reference kernels/expert_cache.hip:626-643 (kernel
+ * :286-314), bound by vllm_expert_cache/_lib.py:50-53, called from cache.py:135-161. */
+EXPERT_CACHE_API int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void* s1,
+                        long b1, void* d2, const void* s2, long b2, void* d3,
+                        const void* s3, long b3, void* d4, const void* s4, long b4,
+                        void* d5, const void* s5, long b5, const int* miss,
+                        const int* n_miss, int chunks, int lanes, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXPERT_CACHE_H */

@@ -1,0 +1,298 @@
+"""Arming logic (backends/generic.py) on CPU stand-ins for vLLM's classes.
+
+The same checks as the reference's tests/test_generic.py:142-352: which per-expert tensors
+are discovered, that the rebuilt quant config is slot-bound, wide steps read through, the
+layer is restored exactly, vLLM's keyword call is accepted, and each refusal fires with a
+reason.  ``cache.refresh`` is replaced by the identity, so no kernel runs.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import pytest
+import torch
+
+from vllm_expert_cache.backends import generic
+
+E, S = 16, 4
+H, N = 8, 12
+
+
+class Log:
+    def __init__(self):
+        self.msgs = []
+
+    def _rec(self, fmt, *a):
+        self.msgs.append(fmt % a if a else fmt)
+
+    warning = info = debug = _rec
+
+    def said(self, needle):
+        return any(needle in m for m in self.msgs)
+
+
+@dataclass
+class Desc:
+    scale: torch.Tensor | None = None
+    alpha_or_gscale: torch.Tensor | None = None
+    zp: torch.Tensor | None = None
+    bias: torch.Tensor | None = None
+
+
+@dataclass
+class QuantConfig:
+    _a1: Desc
+    _a2: Desc
+    _w1: Desc
+    _w2: Desc
+
+
+class FusedExperts:
+    def __init__(self, cfg):
+        self.quant_config = cfg
+
+
+class MoEKernel:
+    def __init__(self, cfg):
+        self.fused_experts = FusedExperts(cfg)
+
+
+class RoutedExperts(torch.nn.Module):
+    """Per-expert tensors as registered Parameters, like vLLM's MoE layer."""
+
+    def __init__(self, extra=(), n_experts=E):
+        super().__init__()
+        p = lambda t: torch.nn.Parameter(t, requires_grad=False)  # noqa: E731
+        self.w13_weight = p(torch.randn(n_experts, N, H))
+        self.w2_weight = p(torch.randn(n_experts, H, N // 2))
+        for name, shape in extra:
+            setattr(self, name, p(torch.randn(*shape)))
+        self.global_num_experts = n_experts
+        self.expert_map = None
+
+
+class QuantMethod:
+    """A FusedMoEMethodBase stand-in whose config factory reads ``reads`` off the layer."""
+
+    is_monolithic = False
+
+    def __init__(self, layer, reads=(), hidden=None):
+        self.reads = list(reads)
+        self.hidden = hidden      # a per-expert tensor the factory returns from nowhere
+        self.moe_quant_config = self._cfg(layer)
+        self.moe_kernel = MoEKernel(self.moe_quant_config)
+        self.seen = None
+
+    def _cfg(self, layer):
+        got = [getattr(layer, n) for n in self.reads]
+        w1 = Desc(scale=got[0] if len(got) > 0 else None, zp=got[2] if len(got) > 2 else None)
+        w2 = Desc(scale=got[1] if len(got) > 1 else None, zp=got[3] if len(got) > 3 else None)
+        if self.hidden is not None:
+            w1.bias = self.hidden
+        return QuantConfig(Desc(), Desc(), w1, w2)
+
+    def get_fused_moe_quant_config(self, layer):
+        return self._cfg(layer)
+
+    def apply(self, layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        self.seen = dict(w13=layer.w13_weight, w2=layer.w2_weight,
+                         cfg=self.moe_kernel.fused_experts.quant_config,
+                         ids=topk_ids.clone(), gne=layer.global_num_experts)
+        return torch.zeros(1)
+
+
+@pytest.fixture(autouse=True)
+def _slots(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_SLOTS", str(S))
+
+
+def arm(layer, method):
+    log = Log()
+    return generic.arm(layer, method, log), log
+
+
+SCALES = [("w13_weight_scale", (E, N, 1)), ("w2_weight_scale", (E, H, 1))]
+
+
+def test_unquantized_mirrors_two_weights():
+    layer = RoutedExperts()
+    ok, _ = arm(layer, QuantMethod(layer))
+    assert ok
+    assert set(layer._expert_cache.names) == {"w13_weight", "w2_weight"}
+
+
+def test_int8_like_mirrors_weights_and_scales():
+    layer = RoutedExperts(SCALES)
+    ok, _ = arm(layer, QuantMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"]))
+    assert ok
+    assert set(layer._expert_cache.names) == {"w13_weight", "w2_weight",
+                                              "w13_weight_scale", "w2_weight_scale"}
+
+
+def test_wna16_like_six_tensors():
+    extra = SCALES + [("w13_weight_zero_point", (E, N, 1)), ("w2_weight_zero_point", (E, H, 1))]
+    layer = RoutedExperts(extra)
+    ok, _ = arm(layer, QuantMethod(layer, reads=[n for n, _ in extra]))
+    assert ok
+    assert len(layer._expert_cache.names) == 6
+
+
+def test_eight_tensors_split_across_gather_launches():
+    extra = SCALES + [(f"aux{i}", (E, 4, 4)) for i in range(4)]
+    layer = RoutedExperts(extra)
+    ok, _ = arm(layer, QuantMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"]))
+    assert ok
+    assert len(layer._expert_cache.names) == 8
+
+
+def test_packed_weights_with_alias():
+    layer = RoutedExperts()
+    for base in ("w13", "w2"):
+        t = getattr(layer, f"{base}_weight")
+        del layer._parameters[f"{base}_weight"]
+        layer.register_parameter(f"{base}_weight_packed", t)
+        setattr(layer, f"{base}_weight", t)        # bare attribute alias, same storage
+    m = QuantMethod(layer)
+    ok, log = arm(layer, m)
+    assert ok, log.msgs
+    cache = layer._expert_cache
+    assert len(cache.slots) == 2
+    assert set(cache.bound) == {"w13_weight", "w13_weight_packed", "w2_weight",
+                                "w2_weight_packed"}
+    assert cache.bound["w13_weight"].data_ptr() == cache.bound["w13_weight_packed"].data_ptr()
+    cache.refresh = lambda ids: ids.clone()
+    m.apply(layer, torch.randn(1, H), torch.ones(1, 2), torch.zeros(1, 2, dtype=torch.int32))
+    assert m.seen["w13"].data_ptr() == cache.slots["w13_weight_packed"].data_ptr()
+    assert layer.w13_weight.data_ptr() == layer.w13_weight_packed.data_ptr()
+
+
+def test_wide_step_reads_through():
+    layer = RoutedExperts(SCALES)
+    m = QuantMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"])
+    assert arm(layer, m)[0]
+    layer._expert_cache.refresh = lambda ids: pytest.fail("wide step must not refresh")
+    m.apply(layer, torch.randn(1, H), torch.ones(1, S + 1),
+            torch.zeros(1, S + 1, dtype=torch.int32))
+    assert m.seen["cfg"]._w1.scale.size(0) == E
+    assert m.seen["gne"] == E
+    assert m.seen["w13"].data_ptr() == layer.w13_weight.data_ptr()
+
+
+def test_slot_binding_reaches_the_config():
+    layer = RoutedExperts(SCALES)
+    m = QuantMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"])
+    assert arm(layer, m)[0]
+    cache = layer._expert_cache
+    cache.refresh = lambda ids: ids.clone() + 100
+    m.apply(layer, torch.randn(1, H), torch.ones(1, 2), torch.zeros(1, 2, dtype=torch.int32))
+    assert m.seen["w13"].data_ptr() == cache.slots["w13_weight"].data_ptr()
+    assert m.seen["cfg"]._w1.scale.size(0) == S
+    assert m.seen["gne"] == S
+    assert (m.seen["ids"] == 100).all()      # apply saw the slot-space ids
+
+
+def test_apply_accepts_keyword_call():
+    layer = RoutedExperts()
+    m = QuantMethod(layer)
+    assert arm(layer, m)[0]
+    layer._expert_cache.refresh = lambda ids: ids.clone()
+    m.apply(layer=layer, x=torch.randn(1, H), topk_weights=torch.ones(1, 2),
+            topk_ids=torch.zeros(1, 2, dtype=torch.int32), shared_experts=None,
+            shared_experts_input=None)
+    assert m.seen is not None
+
+
+def test_layer_is_restored():
+    layer = RoutedExperts(SCALES)
+    m = QuantMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"])
+    names = ("w13_weight", "w2_weight", "w13_weight_scale", "w2_weight_scale")
+    before = {n: getattr(layer, n).data_ptr() for n in names}
+    assert arm(layer, m)[0]
+    layer._expert_cache.refresh = lambda ids: ids.clone()
+    m.apply(layer, torch.randn(1, H), torch.ones(1, 2), torch.zeros(1, 2, dtype=torch.int32))
+    assert {n: getattr(layer, n).data_ptr() for n in names} == before
+    assert layer.global_num_experts == E
+    assert m.moe_kernel.fused_experts.quant_config._w1.scale.size(0) == E
+    assert isinstance(layer._parameters["w13_weight"], torch.nn.Parameter)
+
+
+class FailingMethod(QuantMethod):
+    def apply(self, layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        super().apply(layer, x, topk_weights, topk_ids)
+        raise RuntimeError("stock kernel failed")
+
+
+def test_restored_even_when_apply_raises():
+    layer = RoutedExperts(SCALES)
+    m = FailingMethod(layer, reads=["w13_weight_scale", "w2_weight_scale"])
+    ptr = layer.w13_weight.data_ptr()
+    assert arm(layer, m)[0]
+    layer._expert_cache.refresh = lambda ids: ids.clone()
+    with pytest.raises(RuntimeError, match="stock kernel failed"):
+        m.apply(layer, torch.randn(1, H), torch.ones(1, 2),
+                torch.zeros(1, 2, dtype=torch.int32))
+    assert m.seen["w13"].data_ptr() == layer._expert_cache.slots["w13_weight"].data_ptr()
+    assert layer.w13_weight.data_ptr() == ptr
+    assert layer.global_num_experts == E
+    assert m.moe_kernel.fused_experts.quant_config._w1.scale.size(0) == E
+
+
+def test_hidden_per_expert_tensor_is_refused():
+    layer = RoutedExperts()
+    ok, log = arm(layer, QuantMethod(layer, hidden=torch.randn(E, N)))
+    assert not ok
+    assert log.said("stayed bound to full") and log.said("_w1.bias")
+
+
+def test_monolithic_is_refused():
+    layer = RoutedExperts()
+    m = QuantMethod(layer)
+    m.is_monolithic = True
+    ok, log = arm(layer, m)
+    assert not ok and log.said("monolithic")
+
+
+def test_missing_moe_kernel_is_refused():
+    layer = RoutedExperts()
+    m = QuantMethod(layer)
+    m.moe_kernel = None
+    ok, log = arm(layer, m)
+    assert not ok and log.said("no moe_kernel")
+
+
+def test_expert_parallel_is_refused():
+    layer = RoutedExperts()
+    layer.expert_map = torch.arange(E)
+    ok, log = arm(layer, QuantMethod(layer))
+    assert not ok and log.said("expert parallelism")
+
+
+def test_ragged_auxiliary_is_caught_by_the_leak_check():
+    layer = RoutedExperts([("w13_weight_scale", (E, 3))])        # 12 bytes per expert
+    ok, log = arm(layer, QuantMethod(layer, reads=["w13_weight_scale"]))
+    assert not ok
+    assert log.said("stayed bound to full") and log.said("w13_weight_scale")
+
+
+def test_ragged_weight_is_refused():
+    layer = RoutedExperts()
+    layer.w13_weight = torch.nn.Parameter(torch.randn(E, 3), requires_grad=False)
+    ok, log = arm(layer, QuantMethod(layer))
+    assert not ok
+    assert log.said("multiple of 16") and log.said("w13_weight")
+
+
+def test_nothing_to_cache(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_SLOTS", str(E))
+    layer = RoutedExperts()
+    assert not arm(layer, QuantMethod(layer))[0]
+
+
+def test_unrecognised_weight_names_are_reported():
+    layer = RoutedExperts()
+    layer.register_parameter("w13_qweight_x", layer._parameters.pop("w13_weight"))
+    ok, log = arm(layer, QuantMethod.__new__(QuantMethod))
+    assert not ok and log.said("no recognised expert weight pair")

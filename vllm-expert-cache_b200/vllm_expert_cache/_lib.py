@@ -1,0 +1,58 @@
+"""ctypes binding of libexpertcache.so (the B200 build of the reference's C-ABI).
+
+Search order, as in the reference (vllm_expert_cache/_lib.py:17-33): $EXPERT_CACHE_LIB,
+then ``libexpertcache.so`` beside this package, then /usr/local/lib.  A missing library
+raises FileNotFoundError; there is no fallback path.  The handle is loaded once per
+process.  Argument types are the reference's (_lib.py:41-53) plus the fused-remap entry
+point this build adds.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+# Six (dst, src, bytes) triples per gather call (reference _lib.py:61).
+GATHER_SLOTS = 6
+
+_P, _I, _L = ctypes.c_void_p, ctypes.c_int, ctypes.c_long
+MANAGE_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P]
+MANAGE_REMAP_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P, _I, _P]
+GATHER_ARGTYPES = [_P, _P, _L] * GATHER_SLOTS + [_P, _P, _I, _I, _P]
+
+_handle = None
+
+
+def _candidates():
+    yield os.environ.get("EXPERT_CACHE_LIB")
+    yield str(Path(__file__).resolve().parent / "libexpertcache.so")
+    yield "/usr/local/lib/libexpertcache.so"
+
+
+def library_path() -> str:
+    for cand in _candidates():
+        if cand and Path(cand).is_file():
+            return cand
+    raise FileNotFoundError(
+        "libexpertcache.so not found: build it with "
+        "`python vllm-expert-cache_b200/build_lib.py` (nvcc, sm_100a) so it lands beside "
+        "this package, or set EXPERT_CACHE_LIB to its path.")
+
+
+def bind(h: ctypes.CDLL) -> ctypes.CDLL:
+    h.expert_cache_manage.restype = _I
+    h.expert_cache_manage.argtypes = MANAGE_ARGTYPES
+    h.expert_cache_manage_remap.restype = _I
+    h.expert_cache_manage_remap.argtypes = MANAGE_REMAP_ARGTYPES
+    h.expert_cache_gather.restype = _I
+    h.expert_cache_gather.argtypes = GATHER_ARGTYPES
+    return h
+
+
+def lib() -> ctypes.CDLL:
+    """The bound library, loaded on first use."""
+    global _handle
+    if _handle is None:
+        _handle = bind(ctypes.CDLL(library_path()))
+    return _handle

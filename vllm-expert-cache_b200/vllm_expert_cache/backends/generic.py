@@ -1,0 +1,279 @@
+"""Arming: attach an ExpertSlotCache to every cacheable vLLM MoE layer.
+
+Scheme-agnostic by the same three conventions the reference relies on
+(vllm_expert_cache/backends/generic.py:1-23):
+
+  1. ``method.apply`` reads the expert weights off the layer;
+  2. every per-expert scale / zero point / bias reaches the kernel through
+     ``method.get_fused_moe_quant_config(layer)``, which reads named layer attributes;
+  3. the built kernel keeps that config in ``method.moe_kernel.fused_experts.quant_config``.
+
+So arming discovers the per-expert tensors by shape (dim 0 == E, aliases grouped by
+storage), hangs slot buffers on the layer, re-runs the scheme's own config factory under
+slot binding to get a slot-bound config, refuses the layer if any per-expert tensor
+stayed on full [E] storage, and wraps ``method.apply`` on the instance.  A cached step
+swaps the slot buffers, the slot-bound config and ``global_num_experts = S`` in around the
+original ``apply`` and restores everything afterwards; a step wider than the slots calls
+the original untouched.  The hook is vLLM's single post-load call site,
+``model_loader.utils.process_weights_after_loading``, rebound wherever it was imported by
+name.  Refusals are logged and leave the layer on the stock path.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import itertools
+import sys
+
+import torch
+
+from ..cache import ExpertSlotCache
+from ..config import settings
+
+# FusedMoEQuantConfig descriptors and the fields that can carry a per-expert tensor.
+_QUANT_DESCS = ("_a1", "_a2", "_w1", "_w2")
+_QUANT_FIELDS = ("scale", "alpha_or_gscale", "zp", "bias")
+# Registered names of the two expert weight matrices, plain and packed spellings.
+_WEIGHT_PAIRS = (("w13_weight", "w2_weight"), ("w13_weight_packed", "w2_weight_packed"))
+
+_installed = False
+
+
+def _set_tensor(layer, name: str, t: torch.Tensor) -> None:
+    """Rebind ``layer.<name>`` without tripping nn.Module's Parameter registration."""
+    if name in layer._parameters:
+        layer._parameters[name] = t
+    elif name in layer._buffers:
+        layer._buffers[name] = t
+    else:
+        setattr(layer, name, t)
+
+
+def _per_expert_tensors(layer, num_experts: int) -> dict[str, list[str]]:
+    """Expert-major storages of ``layer``, each with every name that reaches it.
+
+    Registered parameters and buffers are listed without de-duplication (an alias
+    registered under two names must keep both names), then plain tensor attributes
+    (the packed families alias ``w13_weight = w13_weight_packed`` as a bare attribute).
+    Names are grouped by storage so one slot buffer serves every alias; the first name of
+    a group is the one sources are read from.
+    """
+    by_storage: dict[int, list[str]] = {}
+    found = itertools.chain(
+        layer.named_parameters(recurse=False, remove_duplicate=False),
+        layer.named_buffers(recurse=False, remove_duplicate=False),
+        ((k, v) for k, v in vars(layer).items() if isinstance(v, torch.Tensor)))
+    for name, t in found:
+        if not isinstance(t, torch.Tensor) or t.dim() < 1 or t.size(0) != num_experts:
+            continue
+        names = by_storage.setdefault(t.data_ptr(), [])
+        if name not in names:
+            names.append(name)
+    return {names[0]: names for names in by_storage.values()}
+
+
+def _leaked_full_tensors(cfg, num_experts: int) -> list[str]:
+    """Per-expert tensors the slot-bound quant config still holds at full [E] size.
+
+    Such a tensor would be indexed with slot ids and serve the wrong expert's rows, so a
+    non-empty answer refuses the layer.
+    """
+    leaked = []
+    for dname in _QUANT_DESCS:
+        desc = getattr(cfg, dname, None)
+        if desc is None:
+            continue
+        for field in _QUANT_FIELDS:
+            t = getattr(desc, field, None)
+            if isinstance(t, torch.Tensor) and t.dim() >= 1 and t.size(0) == num_experts:
+                leaked.append(f"{dname}.{field}{tuple(t.shape)}")
+    return leaked
+
+
+@contextlib.contextmanager
+def _slot_bound(layer, cache: ExpertSlotCache):
+    """Point every mirrored name at its slot buffer inside the block; restore after."""
+    saved = {name: getattr(layer, name) for name in cache.bound}
+    try:
+        for name, slot in cache.bound.items():
+            _set_tensor(layer, name, slot)
+        yield
+    finally:
+        for name, t in saved.items():
+            _set_tensor(layer, name, t)
+
+
+def _decline(layer, method, num_experts: int) -> str | None:
+    """Why this layer cannot be cached correctly, or None."""
+    if method.is_monolithic:
+        return "monolithic method (routing happens inside apply_monolithic)"
+    kernel = getattr(method, "moe_kernel", None)
+    if kernel is None:
+        return "method has no moe_kernel (legacy non-modular path)"
+    if getattr(kernel, "fused_experts", None) is None:
+        return "moe_kernel exposes no fused_experts to rebind"
+    if getattr(layer, "expert_map", None) is not None:
+        return "expert parallelism active (layer.expert_map is set)"
+    return None
+
+
+def _weight_names(layer) -> tuple[str, str] | None:
+    for pair in _WEIGHT_PAIRS:
+        if all(isinstance(getattr(layer, n, None), torch.Tensor) for n in pair):
+            return pair
+    return None
+
+
+def arm(layer, method, logger) -> bool:
+    """Attach a slot cache to one MoE layer; True when the cache is live."""
+    kind = type(method).__name__
+    names = _weight_names(layer)
+    if names is None:
+        present = sorted(n for n, _ in layer.named_parameters(recurse=False))
+        if any("w13" in n or "w2" in n for n in present):
+            logger.warning("expert-cache: not caching %s -- no recognised expert weight "
+                           "pair; the layer registers %s", kind, ", ".join(present))
+        return False
+    w13_name, w2_name = names
+    num_experts = getattr(layer, w13_name).size(0)
+    slots = settings.slots_for(num_experts)
+    if slots >= num_experts:
+        return False            # everything fits already; a cache would duplicate VRAM
+
+    reason = _decline(layer, method, num_experts)
+    if reason is not None:
+        logger.warning("expert-cache: not caching %s -- %s", kind, reason)
+        return False
+
+    groups = _per_expert_tensors(layer, num_experts)
+    owner_of = {n: canon for canon, group in groups.items() for n in group}
+    for name in (w13_name, w2_name):
+        if name not in owner_of:
+            logger.warning("expert-cache: not caching %s -- %s is not a directly-owned "
+                           "expert-major tensor (found: %s)", kind, name,
+                           ", ".join(sorted(owner_of)) or "none")
+            return False
+    required = set(groups[owner_of[w13_name]]) | set(groups[owner_of[w2_name]])
+    try:
+        cache = ExpertSlotCache(layer, groups.keys(), num_experts, slots,
+                                getattr(layer, w13_name).device, required=required)
+    except ValueError as e:
+        logger.warning("expert-cache: not caching %s -- %s", kind, e)
+        return False
+
+    # One Parameter wrapper per slot storage, shared by all its registered aliases;
+    # plain-attribute aliases get the bare tensor.
+    cache.bound = {}
+    for canon, group in groups.items():
+        if canon not in cache.slots:
+            continue
+        slot = cache.slots[canon]
+        param = torch.nn.Parameter(slot, requires_grad=False)
+        for name in group:
+            cache.bound[name] = param if name in layer._parameters else slot
+    if cache.skipped:
+        logger.info("expert-cache: not mirroring %s (not 16-byte aligned per expert); the "
+                    "leak check decides whether that matters", ", ".join(cache.skipped))
+
+    with _slot_bound(layer, cache):
+        slot_cfg = method.get_fused_moe_quant_config(layer)
+    if slot_cfg is not None:
+        leaked = _leaked_full_tensors(slot_cfg, num_experts)
+        if leaked:
+            logger.warning("expert-cache: not caching %s -- these per-expert tensors "
+                           "stayed bound to full [%d] storage after slot binding and would "
+                           "be indexed by slot id: %s", kind, num_experts, ", ".join(leaked))
+            return False
+
+    stock_apply = method.apply
+
+    # vLLM calls apply by keyword: these parameter names are part of the contract.
+    def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        if not cache.fits(topk_ids):
+            return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
+                               shared_experts_input)
+        slot_ids = cache.refresh(topk_ids)
+        experts = method.moe_kernel.fused_experts
+        saved = (experts.quant_config, method.moe_quant_config, layer.global_num_experts)
+        experts.quant_config = slot_cfg
+        method.moe_quant_config = slot_cfg
+        layer.global_num_experts = cache.S
+        try:
+            with _slot_bound(layer, cache):
+                return stock_apply(layer, x, topk_weights, slot_ids, shared_experts,
+                                   shared_experts_input)
+        finally:
+            experts.quant_config, method.moe_quant_config, layer.global_num_experts = saved
+
+    method.apply = apply
+    layer._expert_cache = cache
+    return True
+
+
+def _arm_model(model, logger, method_base) -> None:
+    armed = declined = 0
+    first = None
+    seen: set[int] = set()
+    for _, module in model.named_modules():
+        method = getattr(module, "quant_method", None)
+        if not isinstance(method, method_base):
+            continue
+        if id(method) in seen:
+            # A quant_method shared by two layers would bind its slot config to the first
+            # layer's buffers and serve the second from them: leave the extras uncached.
+            logger.warning("expert-cache: %s instance is shared across layers; leaving the "
+                           "extra layers uncached", type(method).__name__)
+            declined += 1
+            continue
+        try:
+            if arm(module, method, logger):
+                armed += 1
+                seen.add(id(method))
+                first = first or module._expert_cache
+            else:
+                declined += 1
+        except Exception as e:   # never break serving: the layer keeps the stock path
+            logger.warning("expert-cache: disabled for layer (%r)", e)
+            module._expert_cache = None
+            declined += 1
+    if first is None:
+        logger.info("expert-cache: no cacheable MoE layer found; staying out of the way")
+        return
+    from .. import __version__
+    logger.info("expert-cache %s active on %d MoE layer(s) (%d declined): %d/%d experts "
+                "resident, mirroring %s, policy=%s", __version__, armed, declined, first.S,
+                first.E, "+".join(first.names), settings.policy)
+
+
+def install(logger) -> bool:
+    """Wrap vLLM's post-load hook so every MoE layer is armed once weights are final."""
+    global _installed
+    if _installed:
+        return True
+    try:
+        from vllm.model_executor.layers.fused_moe.fused_moe_method_base import (
+            FusedMoEMethodBase)
+        from vllm.model_executor.model_loader import utils as loader_utils
+    except Exception as e:
+        logger.debug("expert-cache: vLLM MoE interfaces unavailable (%r)", e)
+        return False
+
+    stock = loader_utils.process_weights_after_loading
+
+    def process_weights_after_loading(model, model_config, target_device):
+        stock(model, model_config, target_device)
+        if not settings.disabled:
+            _arm_model(model, logger, FusedMoEMethodBase)
+
+    # base_loader imports the function by name, so rebind every module holding it as
+    # well as the defining module (patching only the latter leaves the hook inert).
+    rebound = []
+    for modname, mod in list(sys.modules.items()):
+        if mod is not None and getattr(mod, "process_weights_after_loading", None) is stock:
+            setattr(mod, "process_weights_after_loading", process_weights_after_loading)
+            rebound.append(modname.rsplit(".", 1)[-1])
+    loader_utils.process_weights_after_loading = process_weights_after_loading
+    logger.info("expert-cache: hooked the MoE loader in %s", ", ".join(rebound) or "utils")
+    _installed = True
+    return True

@@ -1,0 +1,144 @@
+"""Per-MoE-layer expert slot cache: state tensors plus the per-forward step driver.
+
+The full expert tensors stay where vLLM's offloader put them (pinned host memory seen by
+the GPU through UVA); this class adds ``S`` device-resident slots per expert tensor and
+the policy state that decides which experts occupy them.  One cached forward step is:
+
+  1. ``expert_cache_manage_remap`` (one CTA): policy step on the routed ids -- hits
+     refreshed, victims chosen among slots this step does not need, table / miss list
+     rewritten -- and, in the same launch, the routing ids remapped expert -> slot;
+  2. ``expert_cache_gather``: every missing expert's slabs copied from host memory into
+     its new slot (six tensors per launch; wider sets take several launches).
+
+Nothing reads a device value back, so the step is recorded into CUDA graphs like any
+other kernel sequence; every rank that sees the same routing evolves the same state.
+
+Interface and behaviour follow the reference class ``ExpertSlotCache``
+(vllm_expert_cache/cache.py:38-163): constructor arguments, the 16-byte slab rule, the
+``fits`` shape gate, ``remap`` semantics and ``refresh``'s return value.  The difference
+is that the remap runs inside the manage kernel instead of as torch ops.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import GATHER_SLOTS, lib
+from .config import settings
+
+
+def _bytes_per_expert(t: torch.Tensor) -> int:
+    return (t.numel() // t.shape[0]) * t.element_size()
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class ExpertSlotCache:
+    """``num_slots`` of ``num_experts`` experts resident in device memory."""
+
+    def __init__(self, owner, source_names, num_experts: int, num_slots: int, device,
+                 required=()):
+        # Sources are looked up on `owner` at every step: vLLM's offloader moves them to
+        # host memory after weight loading, so a pointer taken here would dangle.
+        self.owner = owner
+        self.names = list(source_names)
+        self.E = int(num_experts)
+        self.S = int(num_slots)
+        self.device = torch.device(device)
+
+        self.slots: dict[str, torch.Tensor] = {}
+        self.skipped: list[str] = []
+        fatal = []
+        for name in self.names:
+            full = getattr(owner, name).data
+            nbytes = _bytes_per_expert(full)
+            if nbytes % 16:
+                # The gather moves 16-byte vectors.  A ragged weight would be handed to
+                # the GEMM half-copied, so it is fatal; a ragged auxiliary tensor is left
+                # unmirrored and the caller's leak check decides whether it matters.
+                where = fatal if name in required else self.skipped
+                where.append(f"{name}{tuple(full.shape)}={nbytes}B")
+                continue
+            self.slots[name] = torch.empty((self.S,) + tuple(full.shape[1:]),
+                                           dtype=full.dtype, device=self.device)
+        if fatal:
+            raise ValueError("per-expert slab must be a multiple of 16 bytes, but these "
+                             "are not: " + ", ".join(fatal))
+        self.names = [n for n in self.names if n in self.slots]
+        # Names -> tensors bound on the layer during a cached step (arming may widen it
+        # with aliases and Parameter wrappers).
+        self.bound: dict[str, torch.Tensor] = dict(self.slots)
+
+        dev = self.device
+        self.table = torch.full((self.E,), -1, dtype=torch.int32, device=dev)
+        self.map_cold = torch.arange(self.E, dtype=torch.int32, device=dev)
+        self.slot_expert = torch.full((self.S,), -1, dtype=torch.int32, device=dev)
+        self.slot_stamp = torch.zeros((self.S,), dtype=torch.int64, device=dev)
+        self.routed = torch.zeros((self.E,), dtype=torch.uint8, device=dev)
+        self.step = torch.zeros((1,), dtype=torch.int64, device=dev)
+        self.miss = torch.zeros((2 * self.S,), dtype=torch.int32, device=dev)
+        self.n_miss = torch.zeros((1,), dtype=torch.int32, device=dev)
+
+        self.policy = settings.policy_code
+        self.decay = settings.decay
+        self.chunks = settings.chunks
+        self.lanes = settings.lanes
+        self._state_args = None
+
+    # ---------------------------------------------------------------------------------
+    def fits(self, topk_ids: torch.Tensor) -> bool:
+        """Can this step be served from slots?  ``tokens x top_k <= S``: shape only, so
+        no device sync; prefill and wide batches fail it and read through."""
+        return topk_ids.numel() <= self.S
+
+    def remap(self, topk_ids: torch.Tensor) -> torch.Tensor:
+        """``table[topk_ids]`` as torch ops (the reference's remap); ``refresh`` does the
+        same inside the manage kernel."""
+        return self.table[topk_ids.to(torch.int64)].to(topk_ids.dtype)
+
+    def _state(self):
+        if self._state_args is None:
+            self._state_args = (
+                _ptr(self.table), _ptr(self.map_cold), _ptr(self.slot_expert),
+                _ptr(self.slot_stamp), _ptr(self.routed), _ptr(self.step),
+                _ptr(self.miss), _ptr(self.n_miss))
+        return self._state_args
+
+    def refresh(self, topk_ids: torch.Tensor) -> torch.Tensor:
+        """Run one cached step and return the routing ids in slot space."""
+        h = lib()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        ids = topk_ids
+        if ids.dtype != torch.int32 or not ids.is_contiguous():
+            ids = ids.to(torch.int32).contiguous()
+        mk = ids.numel()
+        wide = topk_ids.dtype in (torch.int32, torch.int64)
+        out = torch.empty(topk_ids.shape, dtype=topk_ids.dtype if wide else torch.int32,
+                          device=self.device)
+        rc = h.expert_cache_manage_remap(
+            _ptr(ids), mk, self.E, self.S, min(self.E, mk), self.S, *self._state(),
+            self.policy, self.decay, _ptr(out), out.element_size(), stream)
+        if rc != 0:
+            raise RuntimeError(f"expert_cache_manage_remap failed rc={rc}")
+        self._gather(h, stream)
+        return out if wide else out.to(topk_ids.dtype)
+
+    def _gather(self, h, stream) -> None:
+        triples = []
+        for name in self.names:
+            src = getattr(self.owner, name).data
+            triples.append((_ptr(self.slots[name]), _ptr(src),
+                            ctypes.c_long(_bytes_per_expert(src))))
+        for i in range(0, len(triples), GATHER_SLOTS):
+            group = triples[i:i + GATHER_SLOTS]
+            # pad with the group's last triple: the kernel copies a repeated triple once
+            group += [group[-1]] * (GATHER_SLOTS - len(group))
+            args = [x for tr in group for x in tr]
+            rc = h.expert_cache_gather(*args, _ptr(self.miss), _ptr(self.n_miss),
+                                       self.chunks, self.lanes, stream)
+            if rc != 0:
+                raise RuntimeError(f"expert_cache_gather failed rc={rc}")

@@ -1,0 +1,70 @@
+"""Runtime settings, read from the environment on every access.
+
+Names, defaults and quirks are the reference's (vllm_expert_cache/config.py:8-47,
+cache.py:96-97, _lib.py:18, README.md:103-116):
+
+  EXPERT_CACHE_SLOTS      absolute slot count (unset: use FRACTION)
+  EXPERT_CACHE_FRACTION   0.5     fraction of the experts kept resident
+  EXPERT_CACHE_POLICY     lfu     'lfu' (frequency + decay) or 'lru'; anything else -> lru
+  EXPERT_CACHE_DECAY      64      LFU halving period in steps, 0 = never
+  EXPERT_CACHE_DISABLE    0       '1' turns the cache off
+  EXPERT_CACHE_LIB        -       explicit path of libexpertcache.so
+  EXPERT_CACHE_CHUNKS     16      gather CTA budget = CHUNKS * LANES
+  EXPERT_CACHE_LANES      64
+
+``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
+"""
+
+from __future__ import annotations
+
+import os
+
+_POLICIES = {"lru": 0, "lfu": 1}
+
+
+def _env(name: str, default: str | None = None) -> str | None:
+    return os.environ.get(name, default)
+
+
+class Settings:
+    @property
+    def disabled(self) -> bool:
+        return _env("EXPERT_CACHE_DISABLE", "0") == "1"
+
+    @property
+    def slots(self) -> int | None:
+        v = _env("EXPERT_CACHE_SLOTS")
+        return int(v) if v else None
+
+    @property
+    def fraction(self) -> float:
+        return float(_env("EXPERT_CACHE_FRACTION", "0.5"))
+
+    @property
+    def policy(self) -> str:
+        return _env("EXPERT_CACHE_POLICY", "lfu").strip().lower()
+
+    @property
+    def policy_code(self) -> int:
+        return _POLICIES.get(self.policy, 0)
+
+    @property
+    def decay(self) -> int:
+        return int(_env("EXPERT_CACHE_DECAY", "64"))
+
+    @property
+    def chunks(self) -> int:
+        return int(_env("EXPERT_CACHE_CHUNKS", "16"))
+
+    @property
+    def lanes(self) -> int:
+        return int(_env("EXPERT_CACHE_LANES", "64"))
+
+    def slots_for(self, num_experts: int) -> int:
+        want = self.slots
+        if want is None:
+            want = round(num_experts * self.fraction)
+        return max(1, min(int(want), int(num_experts)))
+
+
+settings = Settings()
