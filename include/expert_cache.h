@@ -65,7 +65,7 @@ EXPERT_CACHE_API int expert_cache_manage(const int* topk_ids, int mk, int E, int
  * out_ids[i] = table[topk_ids[i]] on the updated table (torch indexing semantics: a
  * negative id counts from the end; ids outside [-E, E) give -1).  out_ids holds mk
  * elements of out_elem_bytes (4 = int32, 8 = int64) each.  Returns -1 on the manage
- * rules above or when out_ids is NULL / out_elem_bytes is not 4 or 8.
+ * rules above, when out_elem_bytes is not 4 or 8, or when out_ids is NULL and mk > 0.
  *
  * Replaces: the torch remap `table[topk_ids.to(int64)].to(topk_ids.dtype)` of reference
  * vllm_expert_cache/cache.py:108-110 that follows the manage call at :118-163.  It has

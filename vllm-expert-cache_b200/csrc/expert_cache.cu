@@ -408,11 +408,12 @@ int expert_cache_manage_remap(const int* topk_ids, int mk, int E, int S, int max
                               long long* slot_stamp, unsigned char* routed, long long* step,
                               int* miss, int* n_miss, int policy, int decay, void* out_ids,
                               int out_elem_bytes, cudaStream_t stream) {
-  if (out_ids == nullptr || (out_elem_bytes != 4 && out_elem_bytes != 8)) return -1;
+  if ((out_ids == nullptr && mk > 0) || (out_elem_bytes != 4 && out_elem_bytes != 8))
+    return -1;
   ManageArgs a = make_manage_args(topk_ids, mk, E, S, max_distinct, max_inserts, table,
                                   map_cold, slot_expert, slot_stamp, routed, step, miss,
                                   n_miss, policy, decay);
-  a.out_ids = out_ids;
+  a.out_ids = mk > 0 ? out_ids : nullptr;   // nothing to remap: behaves as manage
   a.out_elem_bytes = out_elem_bytes;
   return manage_checked(a, stream);
 }
