@@ -76,6 +76,44 @@ EXPERT_CACHE_API int expert_cache_manage_remap(const int* topk_ids, int mk, int 
                               int* miss, int* n_miss, int policy, int decay, void* out_ids,
                               int out_elem_bytes, cudaStream_t stream);
 
+/* Largest expert count accepted by expert_cache_manage_remap_noalloc: the size, in bytes,
+ * of the library-owned routed-flag array each GPU holds for it. */
+#define EXPERT_CACHE_NOALLOC_MAX_EXPERTS 8192
+
+/* expert_cache_manage_remap for callers that cannot allocate device memory.
+ *
+ * Some callers cannot call cudaMalloc at all: an engine that has already handed every
+ * free byte of HBM to its own pool (a serving stack that sized its KV cache to the card),
+ * a host runtime whose device memory comes only from a foreign allocator, or a latency-
+ * critical loop where cudaMalloc's implicit device-wide synchronisation is not allowed.
+ * The other manage entry points need one caller-allocated scratch array, `routed` (E
+ * bytes); this one takes no `routed` argument and writes those flags into a fixed array
+ * inside the library instead.  Everything else -- ids, state, miss list, out_ids -- is
+ * still passed by the caller, with the same meaning, and the results are identical.
+ *
+ * Limits and rules:
+ *   - E must not exceed EXPERT_CACHE_NOALLOC_MAX_EXPERTS; a larger E returns -2 and
+ *     enqueues nothing.  All other argument errors return -1 as for the other entry
+ *     points.
+ *   - The array is a file-scope device variable: every GPU that loads the library holds
+ *     EXPERT_CACHE_NOALLOC_MAX_EXPERTS bytes for it until the process exits.
+ *   - The first call on each device looks up the array's device address (once, with that
+ *     device current); make that first call before any stream capture begins.
+ *   - Every call on a device shares the one array and leaves the last call's flags in
+ *     it; each call rewrites entries [0, E) before finishing and nothing has to start at
+ *     zero.  Calls that overlap on the GPU (different streams, no ordering between
+ *     them) race on the array's contents; the kernel never reads the array back, so
+ *     their outputs are unaffected, but the array's contents are then unspecified.
+ *   - No cudaMalloc, cudaFree or other allocating call is made.
+ *
+ * Has no counterpart in the reference: the reference's entry points all take `routed`
+ * from the caller. */
+EXPERT_CACHE_API int expert_cache_manage_remap_noalloc(
+    const int* topk_ids, int mk, int E, int S, int max_distinct, int max_inserts, int* table,
+    int* map_cold, int* slot_expert, long long* slot_stamp, long long* step, int* miss,
+    int* n_miss, int policy, int decay, void* out_ids, int out_elem_bytes,
+    cudaStream_t stream);
+
 /* Copy every installed miss's slabs: for j < *n_miss, e = miss[2j], s = miss[2j+1],
  * dst_k[s*b_k .. (s+1)*b_k) = src_k[e*b_k .. (e+1)*b_k) for the six triples.  Sources are
  * usually UVA views of pinned host memory (the copy then streams over the host link).

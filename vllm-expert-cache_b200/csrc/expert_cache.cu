@@ -30,10 +30,16 @@
 // symbols, argument order and return codes (expert_cache.hip:590-645).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 
 #include "expert_cache.h"
+
+// Routed-flag array of expert_cache_manage_remap_noalloc, owned by the library so that
+// entry point allocates nothing.  Host code must not pass this name to a kernel: on the
+// host it is only a stand-in symbol; its device address comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_routed[EXPERT_CACHE_NOALLOC_MAX_EXPERTS];
 
 namespace {
 
@@ -388,6 +394,22 @@ ManageArgs make_manage_args(const int* topk_ids, int mk, int E, int S, int max_d
   return a;
 }
 
+// Device address of g_noalloc_routed on the current device, looked up once per device.
+std::atomic<void*> g_noalloc_routed_addr[kMaxDevices];
+
+int noalloc_routed_address(void** out) {
+  const int dev = current_device();
+  if (dev < 0) return (int)cudaErrorInvalidDevice;
+  void* p = g_noalloc_routed_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_routed);
+    if (err != cudaSuccess) return (int)err;
+    g_noalloc_routed_addr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -416,6 +438,23 @@ int expert_cache_manage_remap(const int* topk_ids, int mk, int E, int S, int max
   a.out_ids = mk > 0 ? out_ids : nullptr;   // nothing to remap: behaves as manage
   a.out_elem_bytes = out_elem_bytes;
   return manage_checked(a, stream);
+}
+
+int expert_cache_manage_remap_noalloc(const int* topk_ids, int mk, int E, int S,
+                                      int max_distinct, int max_inserts, int* table,
+                                      int* map_cold, int* slot_expert, long long* slot_stamp,
+                                      long long* step, int* miss, int* n_miss, int policy,
+                                      int decay, void* out_ids, int out_elem_bytes,
+                                      cudaStream_t stream) {
+  if (E <= 0) return -1;
+  if (E > EXPERT_CACHE_NOALLOC_MAX_EXPERTS) return -2;   // beyond the library's array
+  void* routed = nullptr;
+  const int rc = noalloc_routed_address(&routed);
+  if (rc != 0) return rc;
+  return expert_cache_manage_remap(topk_ids, mk, E, S, max_distinct, max_inserts, table,
+                                   map_cold, slot_expert, slot_stamp,
+                                   static_cast<unsigned char*>(routed), step, miss, n_miss,
+                                   policy, decay, out_ids, out_elem_bytes, stream);
 }
 
 int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void* s1,
