@@ -70,6 +70,7 @@ def parse(argv=None):
     ap.add_argument("--sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-policy-sim", action="store_true")
     a = ap.parse_args(argv)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -445,6 +446,108 @@ def cpu_baseline_port(layer, trace, steps):
     return moved / dt / 1e9, dt
 
 
+def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64):
+    """BASELINE config 1 on the GPU: the 4096-step sticky-Zipf trace through the manage
+    kernel from a cold cache, captured as one CUDA graph of 4096 manage+remap nodes (as
+    vLLM replays them).  Returns device us per layer-step, the graph-node floor (a graph
+    of as many empty kernels), the miss total and the final state."""
+    import torch
+    from vllm_expert_cache import _lib
+    from vllm_expert_cache.synthetic import sticky_zipf_trace
+    h = _lib.lib()
+    E = E_EXPERTS
+    trace = sticky_zipf_trace(seed, steps=steps)
+    mk = trace.shape[1]
+    i32, i64 = torch.int32, torch.int64
+    st = {"table": torch.full((E,), -1, dtype=i32, device=dev),
+          "map_cold": torch.arange(E, dtype=i32, device=dev),
+          "slot_expert": torch.full((S,), -1, dtype=i32, device=dev),
+          "slot_stamp": torch.zeros((S,), dtype=i64, device=dev),
+          "routed": torch.zeros((E,), dtype=torch.uint8, device=dev),
+          "step": torch.zeros((1,), dtype=i64, device=dev),
+          "miss": torch.zeros((2 * S,), dtype=i32, device=dev),
+          "n_miss": torch.zeros((1,), dtype=i32, device=dev)}
+    init = {k: v.clone() for k, v in st.items()}
+    P = ctypes.c_void_p
+    sp = [P(st[k].data_ptr()) for k in ("table", "map_cold", "slot_expert", "slot_stamp",
+                                         "routed", "step", "miss", "n_miss")]
+    ids = torch.from_numpy(trace).to(dev)
+    out = torch.empty_like(ids)
+    nm_hist = torch.zeros(steps, dtype=i32, device=dev)
+
+    def launch(t, stream):
+        rc = h.expert_cache_manage_remap(P(ids[t].data_ptr()), mk, E, S, min(E, mk), S, *sp,
+                                         policy_code, decay, P(out[t].data_ptr()), 4, stream)
+        if rc:
+            raise RuntimeError(f"expert_cache_manage_remap rc={rc}")
+
+    # untimed pass: per-step miss counts
+    stream = P(torch.cuda.current_stream().cuda_stream)
+    for t in range(steps):
+        launch(t, stream)
+        nm_hist[t:t + 1].copy_(st["n_miss"])
+    torch.cuda.synchronize()
+    misses = int(nm_hist.sum().item())
+    final = {k: st[k].cpu().clone() for k in ("table", "map_cold", "slot_expert",
+                                             "slot_stamp", "step")}
+    # timed: the same 4096 steps as one graph, from the same cold state
+    for k, v in init.items():
+        st[k].copy_(v)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        cs = P(side.cuda_stream)
+        for t in range(steps):
+            launch(t, cs)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=side):
+        for t in range(steps):
+            torch.cuda._sleep(0)
+    for warm in (True, False):          # the first replay also uploads the graph
+        for k, v in init.items():
+            st[k].copy_(v)
+        torch.cuda.synchronize()
+        if warm:
+            g.replay()
+            torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / steps
+    for k in final:
+        if not torch.equal(st[k].cpu(), final[k]):
+            raise RuntimeError(f"policy sim: graph replay diverged from the eager pass ({k})")
+    g2.replay()
+    torch.cuda.synchronize()
+    a.record()
+    g2.replay()
+    b.record()
+    torch.cuda.synchronize()
+    floor = a.elapsed_time(b) * 1e3 / steps
+    del g, g2
+    return {"us_per_layer_step": round(us, 3), "graph_node_floor_us": round(floor, 3),
+            "misses": misses, "lookups": int(steps * mk)}, trace, final, nm_hist.cpu().numpy()
+
+
+def policy_sim_cpu_baseline(trace, policy_code, decay, final, nm_gpu, S=64):
+    """The same trace through the C oracle on one core: its time per step, and the check
+    that the GPU's final state and per-step miss counts are the oracle's."""
+    import numpy as np
+    from oracle import policy, policy_c
+    st = policy.CacheState(E_EXPERTS, S)
+    t0 = time.perf_counter()
+    nm = policy_c.run(st, trace, min(E_EXPERTS, trace.shape[1]), S, policy_code, decay)
+    dt = time.perf_counter() - t0
+    same = bool(np.array_equal(nm, nm_gpu)) and all(
+        np.array_equal(final[k].numpy(), getattr(st, k)) for k in final)
+    return {"cpu_us_per_step": round(dt * 1e6 / len(trace), 3), "cpu_cores": 1,
+            "cpu_kind": "port", "parity_with_oracle": same}
+
+
 # ---------------------------------------------------------------------------------------
 
 def run_ours(a, dist):
@@ -522,6 +625,15 @@ def run_ours(a, dist):
                            "unit": "GB/s", "h2d_bytes_per_step": hb,
                            "d2h_bytes_per_step": db,
                            "api": "ExpertSlotCache.refresh (pinned ids in, slot ids out)"}
+        if not a.sweep and not a.no_policy_sim:
+            sim = {"workload": "E128 top-8 S64, 4096 decode steps, sticky Zipf(1.1) "
+                               "p_keep 0.7, seed 0, cold start"}
+            for name, code in (("lfu", 1), ("lru", 0)):
+                res, tr, fin, nm = policy_sim(dev, code, a.decay)
+                if dist.rank == 0 and dist.world == 1 and not a.no_cpu:
+                    res.update(policy_sim_cpu_baseline(tr, code, a.decay, fin, nm))
+                sim[name] = res
+            line["policy_sim"] = sim
         if not a.sweep and not a.no_cpu and dist.rank == 0 and dist.world == 1:
             n = min(K, 200)
             gbs, dt = cpu_baseline_port(layer, trace[W:], n)

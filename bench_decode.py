@@ -1,0 +1,345 @@
+#!/usr/bin/env python
+"""End-to-end decode through vLLM with the expert cache (BASELINE configs 3-5 family).
+
+Synthetic Qwen3-30B-A3B-shaped W8A8 model (48 layers, hidden 2048, 32q/4kv heads of
+128, 128 experts of moe_intermediate 768, top-8, vocab 151936), random-init weights:
+normal(0, 0.02), quantised per output channel to int8 with fp32 scales (compressed-
+tensors "int-quantized", dynamic per-token int8 activations; lm_head and the router stay
+bf16).  Greedy decode at batch 1 from a seeded random 128-token prompt.
+
+Modes, each in its own process (vLLM engine), same weights:
+
+  resident      experts in HBM, cache off                    (the 100% reference)
+  offload       --cpu-offload-params experts, cache off      (vLLM's uncached offload)
+  slots=S       offload + EXPERT_CACHE_SLOTS=S               (the product)
+
+The expert cache is loaded exactly as in production: through its vllm.general_plugins
+entry point.  The synthetic weights come from a load format registered by a second,
+benchmark-only general plugin (`register_synthetic_loader` below), so every vLLM process
+(including tensor-parallel workers) initialises the same deterministic weights.  Both
+entry points are declared in a throw-away site directory put on PYTHONPATH.
+
+Printed: one JSON line per mode (decode tok/s, fraction of resident, tokens identical to
+resident, max |logprob difference| of the chosen tokens) and a summary line.
+
+    python bench_decode.py [--layers 48] [--tp 1] [--slots 16 32 64 96] [--gen 512]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+import zlib
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "vllm-expert-cache_b200"
+LOAD_FORMAT = "synthetic_w8a8"
+
+QWEN3_30B_A3B = {
+    "architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe",
+    "attention_bias": False, "attention_dropout": 0.0,
+    "bos_token_id": 151643, "eos_token_id": 151645, "decoder_sparse_step": 1,
+    "head_dim": 128, "hidden_act": "silu", "hidden_size": 2048,
+    "initializer_range": 0.02, "intermediate_size": 6144, "max_position_embeddings": 4096,
+    "max_window_layers": 48, "mlp_only_layers": [], "moe_intermediate_size": 768,
+    "norm_topk_prob": True, "num_attention_heads": 32, "num_experts": 128,
+    "num_experts_per_tok": 8, "num_hidden_layers": 48, "num_key_value_heads": 4,
+    "output_router_logits": False, "rms_norm_eps": 1e-6, "rope_scaling": None,
+    "rope_theta": 1000000.0, "router_aux_loss_coef": 0.001, "sliding_window": None,
+    "tie_word_embeddings": False, "torch_dtype": "bfloat16", "use_cache": True,
+    "use_sliding_window": False, "vocab_size": 151936,
+}
+
+W8A8_INT8 = {  # int8 weights + dynamic per-token int8 activations
+    "quant_method": "compressed-tensors", "format": "int-quantized",
+    "quantization_status": "compressed", "kv_cache_scheme": None,
+    "global_compression_ratio": None, "ignore": ["lm_head", "re:.*mlp.gate$"],
+    "config_groups": {"group_0": {
+        "targets": ["Linear"], "output_activations": None,
+        "input_activations": {"num_bits": 8, "type": "int", "symmetric": True,
+                              "strategy": "token", "dynamic": True, "group_size": None,
+                              "block_structure": None, "actorder": None,
+                              "observer": None, "observer_kwargs": {}},
+        "weights": {"num_bits": 8, "type": "int", "symmetric": True, "strategy": "channel",
+                    "dynamic": False, "group_size": None, "block_structure": None,
+                    "actorder": None, "observer": "minmax", "observer_kwargs": {}},
+    }},
+}
+
+
+W8A8_FP8 = {   # fp8 e4m3 weights (per channel) + dynamic per-token fp8 activations
+    "quant_method": "compressed-tensors", "format": "float-quantized",
+    "quantization_status": "compressed", "kv_cache_scheme": None,
+    "global_compression_ratio": None, "ignore": ["lm_head", "re:.*mlp.gate$"],
+    "config_groups": {"group_0": {
+        "targets": ["Linear"], "output_activations": None,
+        "input_activations": {"num_bits": 8, "type": "float", "symmetric": True,
+                              "strategy": "token", "dynamic": True, "group_size": None,
+                              "block_structure": None, "actorder": None,
+                              "observer": None, "observer_kwargs": {}},
+        "weights": {"num_bits": 8, "type": "float", "symmetric": True, "strategy": "channel",
+                    "dynamic": False, "group_size": None, "block_structure": None,
+                    "actorder": None, "observer": "minmax", "observer_kwargs": {}},
+    }},
+}
+
+
+def quant_config(kind: str):
+    """``int8``: W8A8 int8 on every Linear; ``int8-experts``: the same with attention left
+    in bf16 (vLLM's CUTLASS int8 scaled-mm does not run on SM100, its fused-MoE int8 path
+    does); ``fp8``: W8A8 fp8; ``bf16``: unquantised."""
+    import copy
+    if kind == "bf16":
+        return None
+    if kind == "fp8":
+        return copy.deepcopy(W8A8_FP8)
+    q = copy.deepcopy(W8A8_INT8)
+    if kind == "int8-experts":
+        q["ignore"] = q["ignore"] + ["re:.*self_attn.*"]
+    return q
+
+
+# ---------------------------------------------------------------------------------------
+# benchmark-only vLLM plugin: deterministic synthetic W8A8 weights
+
+def _seed(name: str, base: int = 1234) -> int:
+    return (base * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFF
+
+
+def init_synthetic_weights(model, std: float = 0.02) -> None:
+    """normal(0, std) everywhere; int8 / fp8 weights quantised per output row with their
+    fp32 ``*_scale`` set to absmax/qmax (127 / 448); norm weights 1."""
+    import torch
+    params = dict(model.named_parameters())
+    quantised = {torch.int8: 127.0, torch.float8_e4m3fn: 448.0}
+    with torch.no_grad():
+        for name, p in params.items():
+            if p.dtype in quantised:
+                qmax = quantised[p.dtype]
+                scale = params.get(name + "_scale")
+                if scale is None:
+                    raise RuntimeError(f"int8 parameter {name} has no {name}_scale")
+                g = torch.Generator(device=p.device).manual_seed(_seed(name))
+                lead = p.shape[0] if p.dim() == 3 else 1
+                qv = p.view(lead, *p.shape[-2:])
+                sv = scale.view(lead, p.shape[-2], -1)
+                for e in range(lead):       # one expert (or one matrix) at a time
+                    w = torch.randn(qv.shape[1:], generator=g, device=p.device,
+                                    dtype=torch.float32) * std
+                    s = w.abs().amax(dim=-1, keepdim=True).clamp_min(1e-8) / qmax
+                    q = (w / s).clamp_(-qmax, qmax)
+                    if p.dtype == torch.int8:
+                        q = torch.round(q)
+                    qv[e].copy_(q.to(p.dtype))
+                    sv[e].copy_(s.to(sv.dtype).expand_as(sv[e]))
+            elif name.endswith("_scale") and name[:-6] in params \
+                    and params[name[:-6]].dtype in quantised:
+                continue                     # written with its weight
+            elif torch.is_floating_point(p):
+                if "norm" in name:
+                    p.fill_(1.0)
+                else:
+                    g = torch.Generator(device=p.device).manual_seed(_seed(name))
+                    p.copy_(torch.randn(p.shape, generator=g, device=p.device,
+                                        dtype=torch.float32).mul_(std).to(p.dtype))
+
+
+def cache_stats_on_worker(worker) -> list:
+    """collective_rpc target: every armed layer's counters (EXPERT_CACHE_STATS=1)."""
+    model = worker.model_runner.get_model()
+    return [m._expert_cache.stats() for m in model.modules()
+            if getattr(m, "_expert_cache", None) is not None]
+
+
+def register_synthetic_loader() -> None:
+    """vllm.general_plugins entry point of the benchmark (not of the product)."""
+    from vllm.model_executor.model_loader import register_model_loader
+    from vllm.model_executor.model_loader.dummy_loader import DummyModelLoader
+
+    class SyntheticW8A8Loader(DummyModelLoader):
+        def load_weights(self, model, model_config) -> None:
+            init_synthetic_weights(model)
+
+    register_model_loader(LOAD_FORMAT)(SyntheticW8A8Loader)
+
+
+# ---------------------------------------------------------------------------------------
+# parent: model directory, plugin site, one child process per mode
+
+def write_model_dir(path: Path, layers: int, max_len: int, quant: str) -> None:
+    cfg = dict(QWEN3_30B_A3B)
+    cfg["num_hidden_layers"] = layers
+    cfg["max_window_layers"] = layers
+    cfg["max_position_embeddings"] = max(max_len, 4096)
+    q = quant_config(quant)
+    if q is not None:
+        cfg["quantization_config"] = q
+    path.mkdir(parents=True, exist_ok=True)
+    (path / "config.json").write_text(json.dumps(cfg, indent=1))
+    (path / "generation_config.json").write_text(json.dumps(
+        {"bos_token_id": 151643, "eos_token_id": 151645, "do_sample": False}))
+
+
+def write_plugin_site(path: Path) -> None:
+    """dist-info entry points for the product plugin and the benchmark loader."""
+    for dist, ep in (("vllm_expert_cache-0.3.0", "expert_cache = vllm_expert_cache:install"),
+                     ("expert_cache_bench-0.0.0",
+                      "synthetic_w8a8 = bench_decode:register_synthetic_loader")):
+        d = path / f"{dist}.dist-info"
+        d.mkdir(parents=True, exist_ok=True)
+        name, ver = dist.rsplit("-", 1)
+        (d / "METADATA").write_text(f"Metadata-Version: 2.1\nName: {name}\nVersion: {ver}\n")
+        (d / "entry_points.txt").write_text(f"[vllm.general_plugins]\n{ep}\n")
+
+
+def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dict:
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join([str(site), str(PKG), str(ROOT),
+                                         env.get("PYTHONPATH", "")])
+    env["VLLM_PLUGINS"] = "expert_cache,synthetic_w8a8"
+    env.pop("EXPERT_CACHE_SLOTS", None)
+    env["EXPERT_CACHE_DISABLE"] = "0" if mode.get("slots") else "1"
+    if mode.get("slots"):
+        env["EXPERT_CACHE_SLOTS"] = str(mode["slots"])
+    env["EXPERT_CACHE_POLICY"] = args.policy
+    env["EXPERT_CACHE_STATS"] = "1"
+    log = logdir / f"decode_{mode['name']}.log"
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--child",
+           json.dumps(mode), "--model", str(model_dir), "--tp", str(args.tp),
+           "--prompt", str(args.prompt), "--gen", str(args.gen), "--seed", str(args.seed)]
+    t0 = time.time()
+    with open(log, "w") as f:
+        rc = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, stderr=f, text=True,
+                            timeout=args.mode_timeout)
+    res = None
+    for line in rc.stdout.splitlines():
+        if line.startswith("{\"decode_result\""):
+            res = json.loads(line)["decode_result"]
+    if rc.returncode != 0 or res is None:
+        tail = log.read_text()[-3000:]
+        raise RuntimeError(f"mode {mode['name']} failed rc={rc.returncode}:\n{tail}")
+    res["wall_s"] = round(time.time() - t0, 1)
+    text = log.read_text()
+    res["armed_log"] = [ln.split("expert-cache", 1)[1].strip()[:160]
+                        for ln in text.splitlines() if "active on" in ln][:1]
+    return res
+
+
+def child(mode: dict, a) -> None:
+    import numpy as np
+    from vllm import LLM, SamplingParams
+    kw = dict(model=a.model, skip_tokenizer_init=True, load_format=LOAD_FORMAT,
+              dtype="bfloat16", tensor_parallel_size=a.tp, max_model_len=a.prompt + a.gen + 16,
+              gpu_memory_utilization=0.55, max_num_seqs=1, seed=a.seed,
+              enable_prefix_caching=False)
+    if mode.get("offload"):
+        kw.update(cpu_offload_gb=mode["offload_gb"], cpu_offload_params={"experts"})
+    t0 = time.time()
+    llm = LLM(**kw)
+    init_s = time.time() - t0
+    rng = np.random.default_rng(a.seed)
+    prompt = {"prompt_token_ids": rng.integers(0, 151936, size=a.prompt).tolist()}
+    greedy = dict(temperature=0.0, ignore_eos=True, detokenize=False)
+    llm.generate([prompt], SamplingParams(max_tokens=32, **greedy), use_tqdm=False)  # warm
+    ref = llm.generate([prompt], SamplingParams(max_tokens=a.gen, logprobs=0, **greedy),
+                       use_tqdm=False)[0].outputs[0]
+    tokens = list(ref.token_ids)
+    lps = [float(d[t].logprob) for d, t in zip(ref.logprobs, tokens)]
+    times = {}
+    for n in (1, a.gen):
+        best = None
+        for _ in range(2):
+            t = time.perf_counter()
+            llm.generate([prompt], SamplingParams(max_tokens=n, **greedy), use_tqdm=False)
+            dt = time.perf_counter() - t
+            best = dt if best is None else min(best, dt)
+        times[n] = best
+    decode_tps = (a.gen - 1) / (times[a.gen] - times[1])
+    cache = None
+    if mode.get("slots"):
+        per_rank = llm.collective_rpc(cache_stats_on_worker)
+        layers = per_rank[0] if per_rank else []
+        if layers:
+            steps = sum(x["steps"] for x in layers)
+            installs = sum(x.get("installs", 0) for x in layers)
+            cache = {"armed_layers": len(layers), "layer_steps": steps, "installs": installs,
+                     "installs_per_layer_step": round(installs / max(steps, 1), 4),
+                     "bytes_per_install": layers[0].get("bytes_per_install")}
+    out = {"mode": mode["name"], "slots": mode.get("slots"), "offload": bool(mode.get("offload")),
+           "tp": a.tp, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
+           "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
+           "cache": cache, "tokens": tokens, "logprobs": lps}
+    print(json.dumps({"decode_result": out}), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--slots", type=int, nargs="*", default=[16, 32, 64, 96])
+    ap.add_argument("--prompt", type=int, default=128)
+    ap.add_argument("--gen", type=int, default=512)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--policy", default="lfu")
+    ap.add_argument("--quant", choices=["int8", "int8-experts", "fp8", "bf16"],
+                    default="int8-experts")
+    ap.add_argument("--offload-gb", type=float, default=64.0)
+    ap.add_argument("--no-offload-baseline", action="store_true")
+    ap.add_argument("--mode-timeout", type=int, default=1200)
+    ap.add_argument("--logdir", default="gpurun_out")
+    ap.add_argument("--child", default=None)
+    ap.add_argument("--model", default=None)
+    a = ap.parse_args(argv)
+    if a.child:
+        return child(json.loads(a.child), a)
+
+    logdir = Path(a.logdir)
+    logdir.mkdir(parents=True, exist_ok=True)
+    tmp = Path(tempfile.mkdtemp(prefix="expert_cache_decode_"))
+    model_dir, site = tmp / "model", tmp / "site"
+    write_model_dir(model_dir, a.layers, a.prompt + a.gen + 16, a.quant)
+    write_plugin_site(site)
+    modes = [{"name": "resident"}]
+    if not a.no_offload_baseline:
+        modes.append({"name": "offload", "offload": True, "offload_gb": a.offload_gb})
+    modes += [{"name": f"slots{s}", "slots": s, "offload": True, "offload_gb": a.offload_gb}
+              for s in a.slots]
+    results = []
+    base = None
+    for m in modes:
+        r = run_mode(m, a, model_dir, site, logdir)
+        if base is None:
+            base = r
+        r["frac_of_resident"] = round(r["decode_tok_s"] / base["decode_tok_s"], 4)
+        r["tokens_match_resident"] = r["tokens"] == base["tokens"]
+        first = next((i for i, (x, y) in enumerate(zip(r["tokens"], base["tokens"]))
+                      if x != y), None)
+        r["first_divergent_token"] = first
+        upto = len(r["tokens"]) if first is None else first + 1
+        r["max_abs_logprob_diff"] = max(
+            (abs(x - y) for x, y in zip(r["logprobs"][:upto], base["logprobs"][:upto])),
+            default=0.0)
+        slim = {k: v for k, v in r.items() if k not in ("tokens", "logprobs")}
+        slim.update(layers=a.layers, prompt=a.prompt, gen=a.gen, policy=a.policy,
+                    quant=a.quant)
+        print(json.dumps(slim), flush=True)
+        results.append(slim)
+    # greedy tokens identical to resident, and the chosen tokens' logprobs within 1e-2
+    # (up to and including the first divergent position when tokens differ)
+    ok = all(r["tokens_match_resident"] and r["max_abs_logprob_diff"] <= 1e-2
+             for r in results)
+    print(json.dumps({"summary": "decode", "all_match_resident_within_1e-2": ok,
+                      "decode_tok_s": {r["mode"]: r["decode_tok_s"] for r in results},
+                      "frac_of_resident": {r["mode"]: r["frac_of_resident"] for r in results}}),
+          flush=True)
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main() or 0)

@@ -268,9 +268,13 @@ def install(logger) -> bool:
 
     # base_loader imports the function by name, so rebind every module holding it as
     # well as the defining module (patching only the latter leaves the hook inert).
+    # Module dicts are read directly: getattr on lazy modules (transformers') would
+    # import or alias-resolve names as a side effect.
     rebound = []
     for modname, mod in list(sys.modules.items()):
-        if mod is not None and getattr(mod, "process_weights_after_loading", None) is stock:
+        namespace = getattr(mod, "__dict__", None) if mod is not None else None
+        if isinstance(namespace, dict) and \
+                namespace.get("process_weights_after_loading") is stock:
             setattr(mod, "process_weights_after_loading", process_weights_after_loading)
             rebound.append(modname.rsplit(".", 1)[-1])
     loader_utils.process_weights_after_loading = process_weights_after_loading

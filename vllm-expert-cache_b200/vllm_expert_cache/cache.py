@@ -83,6 +83,10 @@ class ExpertSlotCache:
         self.miss = torch.zeros((2 * self.S,), dtype=torch.int32, device=dev)
         self.n_miss = torch.zeros((1,), dtype=torch.int32, device=dev)
 
+        # Opt-in counter: installs summed over every cached step (device int64, no sync).
+        self.miss_total = (torch.zeros((1,), dtype=torch.int64, device=dev)
+                           if settings.stats else None)
+
         self.policy = settings.policy_code
         self.decay = settings.decay
         self.chunks = settings.chunks
@@ -124,8 +128,19 @@ class ExpertSlotCache:
             self.policy, self.decay, _ptr(out), out.element_size(), stream)
         if rc != 0:
             raise RuntimeError(f"expert_cache_manage_remap failed rc={rc}")
+        if self.miss_total is not None:
+            self.miss_total.add_(self.n_miss)
         self._gather(h, stream)
         return out if wide else out.to(topk_ids.dtype)
+
+    def stats(self) -> dict:
+        """Host snapshot of the counters (synchronises; call outside the hot path)."""
+        out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item())}
+        if self.miss_total is not None:
+            out["installs"] = int(self.miss_total.item())
+            out["bytes_per_install"] = sum(_bytes_per_expert(getattr(self.owner, n).data)
+                                           for n in self.names)
+        return out
 
     def _gather(self, h, stream) -> None:
         triples = []

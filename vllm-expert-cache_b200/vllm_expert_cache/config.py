@@ -11,6 +11,9 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
   EXPERT_CACHE_LIB        -       explicit path of libexpertcache.so
   EXPERT_CACHE_CHUNKS     16      gather CTA budget = CHUNKS * LANES
   EXPERT_CACHE_LANES      64
+  EXPERT_CACHE_STATS      0       '1' keeps a device-side running total of installs per
+                                  layer (one extra tiny kernel per cached step; new in
+                                  this build, off by default)
 
 ``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
 """
@@ -59,6 +62,10 @@ class Settings:
     @property
     def lanes(self) -> int:
         return int(_env("EXPERT_CACHE_LANES", "64"))
+
+    @property
+    def stats(self) -> bool:
+        return _env("EXPERT_CACHE_STATS", "0") == "1"
 
     def slots_for(self, num_experts: int) -> int:
         want = self.slots
