@@ -236,7 +236,8 @@ class Layer:
                                   dtype=self.host[n].dtype, device=device)
                       for n in self.names]
         self.bytes_per_expert = sum(self.sizes)
-        rng = __import__("numpy").random.default_rng(seed + 1000)
+        import numpy as np
+        rng = np.random.default_rng(seed + 1000)
         self.hot = sorted(rng.choice(self.E, size=S, replace=False).tolist())
         i32, i64 = torch.int32, torch.int64
         self.state = {
@@ -598,7 +599,9 @@ def run_ours(a, dist):
                 "experts": E_EXPERTS, "slots": S, "misses_per_step": m,
                 "tokens_per_step": T, "top_k": TOP_K,
                 "bytes_per_expert": layer.bytes_per_expert, "policy": a.policy,
-                "decay": a.decay, "gather_ctas": chunks * lanes,
+                "decay": a.decay,
+                "gather_ctas": min(chunks * lanes,
+                                   2 * torch.cuda.get_device_properties(dev).multi_processor_count),
                 "l2": f"inputs larger than L2: {E_EXPERTS * layer.bytes_per_expert >> 20} "
                       f"MiB host experts, {S * layer.bytes_per_expert >> 20} MiB slots "
                       f"(L2 {L2_BYTES >> 20} MiB)",

@@ -76,6 +76,39 @@ EXPERT_CACHE_API int expert_cache_manage_remap(const int* topk_ids, int mk, int 
                               int* miss, int* n_miss, int policy, int decay, void* out_ids,
                               int out_elem_bytes, cudaStream_t stream);
 
+/* Largest expert count of expert_cache_fused (reference expert_cache.hip:341, MAXE). */
+#define EXPERT_CACHE_FUSED_MAX_EXPERTS 1024
+
+/* Manage step fused with both of vLLM's moe_align_block_size outputs, in one launch.
+ *
+ * The manage part is expert_cache_manage with LRU priorities and no ageing (the
+ * reference's fused path has no policy argument).  Then, on the updated table, the
+ * routing ids are bucketed twice, as moe_align_block_size(topk_ids, bs, ..., map,
+ * ignore_invalid_experts=True) would:
+ *   hot  side: tokens whose expert is resident, bucket = its SLOT (table[e]);
+ *   cold side: the others, bucket = the expert id (map_cold[e]).
+ * For each side: sorted_* [L] holds token indices grouped by bucket, each bucket padded
+ * to a multiple of bs with the sentinel mk; eids_* [NB] holds the bucket of each block
+ * (-1 for unused blocks); npad_* [1] the padded total.  Tokens inside a bucket are in
+ * ascending index order for every mk (the reference guarantees that only for mk <= 256).
+ * L and NB must be the lengths vLLM's wrapper allocates:
+ *   L = mk < E ? min(mk*bs, mk + E*(bs-1)) : mk + E*(bs-1);  NB = ceil(L / bs);
+ * writes past L / NB are dropped rather than made.
+ *
+ * Returns -1 if E <= 0, E > EXPERT_CACHE_FUSED_MAX_EXPERTS, S <= 0,
+ * S > EXPERT_CACHE_MAX_SLOTS, bs/L/NB <= 0, mk < 0 or max_inserts outside
+ * [0, EXPERT_CACHE_MAX_INSERTS].
+ *
+ * Replaces: expert_cache_fused, reference kernels/expert_cache.hip:610-624 (kernel
+ * :431-588); exported there and checked by kernels/build.sh:36-38, not called by the
+ * reference's Python. */
+EXPERT_CACHE_API int expert_cache_fused(
+    const int* topk_ids, int mk, int E, int S, int max_distinct, int max_inserts, int* table,
+    int* map_cold, int* slot_expert, long long* slot_stamp, unsigned char* routed,
+    long long* step, int* miss, int* n_miss, int bs, int L, int NB, int* sorted_hot,
+    int* eids_hot, int* npad_hot, int* sorted_cold, int* eids_cold, int* npad_cold,
+    cudaStream_t stream);
+
 /* Largest expert count accepted by expert_cache_manage_remap_noalloc: the size, in bytes,
  * of the library-owned routed-flag array each GPU holds for it. */
 #define EXPERT_CACHE_NOALLOC_MAX_EXPERTS 8192
@@ -118,7 +151,8 @@ EXPERT_CACHE_API int expert_cache_manage_remap_noalloc(
  * dst_k[s*b_k .. (s+1)*b_k) = src_k[e*b_k .. (e+1)*b_k) for the six triples.  Sources are
  * usually UVA views of pinned host memory (the copy then streams over the host link).
  * Identical triples (the caller's padding) are copied once.  chunks * lanes is the CTA
- * budget of the launch (defaults 16 * 64 in the reference's Python layer).
+ * budget of the launch (defaults 16 * 64 in the reference's Python layer); the launch
+ * uses min(budget, 2 * SM count) CTAs.
  *
  * Returns -1 if any b_k <= 0 or b_k % 16, any dst/src not 16-byte aligned, or
  * chunks <= 0 / lanes <= 0.

@@ -196,3 +196,53 @@ def check_invariants(st: CacheState) -> list[str]:
     if len(live) and not (t[live] == live_slots).all():
         bad.append("table/slot mismatch")
     return bad
+
+
+def align_lengths(mk: int, E: int, bs: int) -> tuple[int, int]:
+    """(L, NB): the buffer lengths vLLM's moe_align_block_size wrapper allocates for mk
+    routing ids over E experts (vllm/model_executor/layers/fused_moe/
+    moe_align_block_size.py:74-84; the reference's fused launcher comment,
+    kernels/expert_cache.hip:606-609)."""
+    L = mk + E * (bs - 1)
+    if mk < E:
+        L = min(mk * bs, L)
+    return L, (L + bs - 1) // bs
+
+
+def align(table: np.ndarray, ids, S: int, bs: int, L: int, NB: int):
+    """Both moe_align_block_size outputs of the fused step, on the UPDATED table.
+
+    Token i with a valid expert e goes to the hot side in bucket table[e] when
+    0 <= table[e] < S, else to the cold side in bucket e (map_cold's value for a
+    non-resident expert).  Per side: buckets in ascending order, each padded to a multiple
+    of ``bs`` with the sentinel mk; tokens inside a bucket in ascending index; block ->
+    bucket ids, -1 for unused blocks; the padded total.  Restates the reference's fused
+    kernel phases 1-5 (kernels/expert_cache.hip:515-587) with deterministic placement.
+    Returns (sorted_hot, eids_hot, npad_hot, sorted_cold, eids_cold, npad_cold).
+    """
+    ids = np.asarray(ids).reshape(-1).astype(np.int64)
+    E = table.shape[0]
+    mk = ids.size
+    hot = [[] for _ in range(S)]
+    cold = [[] for _ in range(E)]
+    for i, e in enumerate(ids.tolist()):
+        if e < 0 or e >= E:
+            continue
+        s = int(table[e])
+        (hot[s] if 0 <= s < S else cold[e]).append(i)
+    out = []
+    for buckets in (hot, cold):
+        sorted_ids = np.full(L, mk, dtype=np.int32)
+        eids = np.full(NB, -1, dtype=np.int32)
+        pos = 0
+        for b, toks in enumerate(buckets):
+            padded = -(-len(toks) // bs) * bs
+            for k, tok in enumerate(toks):
+                if pos + k < L:
+                    sorted_ids[pos + k] = tok
+            for blk in range(pos // bs, (pos + padded) // bs):
+                if blk < NB:
+                    eids[blk] = b
+            pos += padded
+        out += [sorted_ids, eids, np.array([pos], dtype=np.int32)]
+    return tuple(out)

@@ -77,37 +77,12 @@ def compare_state(ds_host: dict, st: CacheState, nins: int, tag: str) -> None:
     np.testing.assert_array_equal(got[1:2 * n:2], want[1:2 * n:2], err_msg=f"{tag}: miss slots")
 
 
-class _CudaArray:
-    def __init__(self, ptr, shape, typestr):
-        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
-                                         "data": (ptr, False), "version": 3, "strides": None}
-
-
-_TYPESTR = {torch.int8: "|i1", torch.uint8: "|u1", torch.float32: "<f4",
-            torch.bfloat16: "<V2", torch.int32: "<i4", torch.float16: "<f2"}
-
-
-def cudart():
-    torch.cuda.init()
-    rt = ctypes.CDLL("libcudart.so.12")
-    rt.cudaHostGetDevicePointer.restype = ctypes.c_int
-    rt.cudaHostGetDevicePointer.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p,
-                                            ctypes.c_uint]
-    return rt
-
-
 def device_ptr_of_pinned(host: torch.Tensor) -> int:
-    assert host.is_pinned()
-    dp = ctypes.c_void_p()
-    rc = cudart().cudaHostGetDevicePointer(ctypes.byref(dp), ctypes.c_void_p(host.data_ptr()), 0)
-    assert rc == 0, f"cudaHostGetDevicePointer rc={rc}"
-    return dp.value
+    from vllm_expert_cache.synthetic import host_device_pointer
+    return host_device_pointer(host)
 
 
 def uva_view(host: torch.Tensor) -> torch.Tensor:
     """A CUDA tensor aliasing pinned host memory (reads cross the host link)."""
-    dptr = device_ptr_of_pinned(host)
-    if host.dtype == torch.bfloat16:
-        v = torch.as_tensor(_CudaArray(dptr, host.shape, "<i2"), device=DEV)
-        return v.view(torch.bfloat16)
-    return torch.as_tensor(_CudaArray(dptr, host.shape, _TYPESTR[host.dtype]), device=DEV)
+    from vllm_expert_cache.synthetic import uva_view as _view
+    return _view(host, DEV)

@@ -131,3 +131,19 @@ def test_install_respects_disable(monkeypatch):
     import vllm_expert_cache
     monkeypatch.setenv("EXPERT_CACHE_DISABLE", "1")
     vllm_expert_cache.install()   # returns without importing vLLM's loader
+
+
+def fused(h, E=8, S=4, mi=4, mk=2, bs=16, L=32, NB=2):
+    return h.expert_cache_fused(NULL, mk, E, S, 8, mi, *([NULL] * 8), bs, L, NB,
+                                *([NULL] * 6), NULL)
+
+
+@pytest.mark.parametrize("kw", [dict(E=0), dict(E=1025), dict(S=0), dict(S=1025),
+                                dict(bs=0), dict(L=0), dict(NB=0), dict(mk=-1),
+                                dict(mi=-1), dict(mi=1025)])
+def test_fused_refuses_bad_arguments(h, kw):
+    import ctypes as C
+    P, I = C.c_void_p, C.c_int
+    h.expert_cache_fused.restype = I
+    h.expert_cache_fused.argtypes = [P] + [I] * 5 + [P] * 8 + [I, I, I] + [P] * 6 + [P]
+    assert fused(h, **kw) == -1

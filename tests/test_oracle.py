@@ -154,3 +154,33 @@ def test_c_oracle_agrees_with_python_oracle_on_random_cases():
                 np.testing.assert_array_equal(v, getattr(b, k), err_msg=k)
             nins = int(a.n_miss[0])
             np.testing.assert_array_equal(a.miss[:2 * nins], b.miss[:2 * nins])
+
+
+def test_align_oracle_small_known_answer():
+    """vLLM's documented example (moe_align_block_size.py:59-72), all experts cold: the
+    cold side must reproduce it; the hot side is then empty."""
+    table = np.full(5, -1, dtype=np.int32)            # experts 0..4, none resident
+    ids = np.array([2, 3, 4, 1, 2, 4, 1, 3, 4, 1, 2, 3], dtype=np.int32)
+    L, NB = policy.align_lengths(12, 5, 4)
+    sh, eh, nh, sc, ec, nc = policy.align(table, ids, 4, 4, L, NB)
+    assert nh[0] == 0 and (eh == -1).all() and (sh == 12).all()
+    assert nc[0] == 16
+    np.testing.assert_array_equal(sc[:16], [3, 6, 9, 12, 0, 4, 10, 12, 1, 7, 11, 12,
+                                            2, 5, 8, 12])
+    np.testing.assert_array_equal(ec[:4], [1, 2, 3, 4])
+
+
+def test_align_oracle_hot_cold_split():
+    table = np.array([-1, 2, -1, 0, -1, 1], dtype=np.int32)   # experts 1,3,5 resident
+    ids = np.array([[1, 0], [3, 5], [0, 1], [-1, 4]], dtype=np.int32)
+    L, NB = policy.align_lengths(8, 6, 2)
+    sh, eh, nh, sc, ec, nc = policy.align(table, ids, 3, 2, L, NB)
+    # hot buckets by slot: slot0 <- expert3 (token 2), slot1 <- expert5 (3), slot2 <- 1 (0,5)
+    assert nh[0] == 6
+    np.testing.assert_array_equal(sh[:6], [2, 8, 3, 8, 0, 5])
+    np.testing.assert_array_equal(eh[:3], [0, 1, 2])
+    # cold buckets by expert: 0 (tokens 1, 4), 4 (token 7)
+    assert nc[0] == 4
+    np.testing.assert_array_equal(sc[:4], [1, 4, 7, 8])
+    np.testing.assert_array_equal(ec[:2], [0, 4])
+    assert (ec[2:] == -1).all()

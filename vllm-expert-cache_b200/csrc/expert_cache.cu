@@ -96,31 +96,51 @@ __device__ __forceinline__ void remap_tail(const int* __restrict__ ids, int mk, 
   }
 }
 
-// NT threads; requires S <= NT.  Thread t owns slot t; experts are processed in tiles of
-// NT (thread t owns expert base + t), in ascending id.
+// Shared-memory views of one manage call (layout: manage_smem_bytes).
+struct ManageSmem {
+  long long* key;        // [spad] eviction keys
+  long long* stamp;      // [spad] priorities after hits / ageing
+  int* table;            // [E] expert -> slot, updated by the installs
+  int* slot_expert;      // [S]
+  unsigned char* flag;   // [E] routed this step
+};
+
+__device__ __forceinline__ ManageSmem manage_smem(unsigned char* base, int E, int S) {
+  const int spad = (S + 1) & ~1;
+  ManageSmem m;
+  m.key = reinterpret_cast<long long*>(base);
+  m.stamp = m.key + spad;
+  m.table = reinterpret_cast<int*>(m.stamp + spad);
+  m.slot_expert = m.table + E;
+  m.flag = reinterpret_cast<unsigned char*>(m.slot_expert + S);
+  return m;
+}
+
+// One policy step for the whole CTA (NT threads, S <= NT).  Thread t owns slot t; experts
+// are processed in tiles of NT (thread t owns expert base + t), in ascending id.  All
+// global state is read once into shared memory and written back directly.  On return
+// `sm.table` holds the updated expert->slot table, but only for the installing threads'
+// own writes: the caller needs a CTA barrier before reading it when this returns true
+// (true = installs happened).  `my_id` is topk_ids[t] (or -1 when t >= mk).
 template <int NT>
-__global__ void __launch_bounds__(NT) manage_kernel(const __grid_constant__ ManageArgs a) {
+__device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSmem& sm,
+                                            int my_id) {
   constexpr int NW = NT / 32;
-  extern __shared__ __align__(16) unsigned char smem[];
   __shared__ int s_missing[EXPERT_CACHE_MAX_INSERTS];   // r-th missing expert, ascending
   __shared__ int w_routed[2][NW], w_missed[2][NW], w_evict[NW];
 
   const int E = a.E, S = a.S;
   const int spad = (S + 1) & ~1;
-  long long* s_key = reinterpret_cast<long long*>(smem);
-  long long* s_st = s_key + spad;
-  int* s_tab = reinterpret_cast<int*>(s_st + spad);
-  int* s_se = s_tab + E;
-  unsigned char* s_flag = reinterpret_cast<unsigned char*>(s_se + S);
+  long long* s_key = sm.key;
+  long long* s_st = sm.stamp;
+  int* s_tab = sm.table;
+  int* s_se = sm.slot_expert;
+  unsigned char* s_flag = sm.flag;
 
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
 
-  grid_dependency_wait();     // topk_ids may come from the kernel just before us
-  release_dependents();       // let the gather launch and park on its own wait
-
-  // ---- one round of loads: ids, step, table, slot state --------------------------------
+  // ---- one round of loads: step, table, slot state (ids were read by the caller) -------
   const long long now = a.step[0] + 1;
-  const int my_id = (t < a.mk) ? a.ids[t] : -1;
   for (int e = t; e < E; e += NT) {
     s_tab[e] = a.table[e];
     s_flag[e] = 0;
@@ -198,8 +218,7 @@ __global__ void __launch_bounds__(NT) manage_kernel(const __grid_constant__ Mana
     // keep their refreshed priority and no ageing runs (it only runs on inserting steps).
     if (!read_through && hit) a.slot_stamp[t] = stamp;
     if (t == 0) a.n_miss[0] = 0;
-    if (a.out_ids) remap_tail(a.ids, a.mk, E, a.out_ids, a.out_elem_bytes, s_tab, my_id, NT);
-    return;
+    return false;
   }
 
   // ---- ageing, eviction keys, miss list -------------------------------------------------
@@ -251,9 +270,173 @@ __global__ void __launch_bounds__(NT) manage_kernel(const __grid_constant__ Mana
     }
   }
   if (t == 0) a.n_miss[0] = min(nins, n_evict);
+  return true;
+}
+
+// expert_cache_manage / expert_cache_manage_remap: the policy step, then (optionally) the
+// remap of the routing ids on the updated table.
+template <int NT>
+__global__ void __launch_bounds__(NT, 1) manage_kernel(const __grid_constant__ ManageArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const ManageSmem sm = manage_smem(smem, a.E, a.S);
+  grid_dependency_wait();     // topk_ids may come from the kernel just before us
+  release_dependents();       // let the gather launch and park on its own wait
+  const int t = threadIdx.x;
+  const int my_id = (t < a.mk) ? a.ids[t] : -1;
+  const bool changed = manage_core<NT>(a, sm, my_id);
   if (a.out_ids) {
-    __syncthreads();
-    remap_tail(a.ids, a.mk, E, a.out_ids, a.out_elem_bytes, s_tab, my_id, NT);
+    if (changed) __syncthreads();
+    remap_tail(a.ids, a.mk, a.E, a.out_ids, a.out_elem_bytes, sm.table, my_id, NT);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// fused: manage + both moe_align_block_size outputs (reference expert_cache.hip:316-588)
+
+struct AlignArgs {
+  int bs, L, NB;
+  int* sorted_hot;
+  int* eids_hot;
+  int* npad_hot;
+  int* sorted_cold;
+  int* eids_cold;
+  int* npad_cold;
+};
+
+// Extra dynamic shared memory after the manage layout: cnt_h[S] cum_h[S+1] cnt_c[E]
+// cum_c[E+1] (ints).
+__host__ __device__ inline size_t fused_smem_bytes(int E, int S) {
+  return manage_smem_bytes(E, S) + (size_t)(2 * S + 2 * E + 2) * 4 + 16;
+}
+
+// Exclusive scan of one value per thread across the CTA; *total gets the CTA sum.  The
+// caller separates two uses of `warp_buf` with a barrier.
+template <int NT>
+__device__ __forceinline__ int cta_exclusive_scan(int v, int* warp_buf, int* total) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_buf[w] = x;
+  __syncthreads();
+  int before = 0, sum = 0;
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    const int c = warp_buf[k];
+    before += (k < w) ? c : 0;
+    sum += c;
+  }
+  *total = sum;
+  return before + x - v;
+}
+
+// cum[b] = sum over j < b of roundup(cnt[j], bs); cum[n] = total.  Thread t owns the
+// contiguous buckets [t*C, t*C + C).
+template <int NT>
+__device__ __forceinline__ void padded_scan(const int* cnt, int* cum, int n, int bs,
+                                            int* warp_buf) {
+  const int C = (n + NT - 1) / NT;
+  const int lo = threadIdx.x * C, hi = min(lo + C, n);
+  int mine = 0;
+  for (int b = lo; b < hi; ++b) mine += (cnt[b] + bs - 1) / bs * bs;
+  int total = 0;
+  int run = cta_exclusive_scan<NT>(mine, warp_buf, &total);
+  for (int b = lo; b < hi; ++b) {
+    cum[b] = run;
+    run += (cnt[b] + bs - 1) / bs * bs;
+  }
+  if (threadIdx.x == 0) cum[n] = total;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(NT, 1)
+    fused_kernel(const __grid_constant__ ManageArgs a, const __grid_constant__ AlignArgs g) {
+  constexpr int NW = NT / 32;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int warp_h[NW], warp_c[NW];
+  const int E = a.E, S = a.S, mk = a.mk;
+  const ManageSmem sm = manage_smem(smem, E, S);
+  int* cnt_h = reinterpret_cast<int*>(smem + manage_smem_bytes(E, S) + 16 -
+                                      (manage_smem_bytes(E, S) & 15));
+  int* cum_h = cnt_h + S;
+  int* cnt_c = cum_h + S + 1;
+  int* cum_c = cnt_c + E;
+  const int t = threadIdx.x, lane = t & 31;
+
+  grid_dependency_wait();
+  release_dependents();
+  const int my_id = (t < mk) ? a.ids[t] : -1;
+  manage_core<NT>(a, sm, my_id);   // LRU semantics: the launcher passes policy 0
+
+  // ---- sentinels, cleared counts ---------------------------------------------------------
+  for (int i = t; i < g.L; i += NT) {
+    g.sorted_hot[i] = mk;
+    g.sorted_cold[i] = mk;
+  }
+  for (int i = t; i < g.NB; i += NT) {
+    g.eids_hot[i] = -1;
+    g.eids_cold[i] = -1;
+  }
+  for (int b = t; b < S; b += NT) cnt_h[b] = 0;
+  for (int b = t; b < E; b += NT) cnt_c[b] = 0;
+  __syncthreads();   // also publishes the installs' table updates
+
+  // ---- one counting pass feeds both sides: resident -> slot bucket, else expert bucket --
+  for (int i = t; i < mk; i += NT) {
+    const int e = (i == t) ? my_id : a.ids[i];
+    if (e < 0 || e >= E) continue;
+    const int s = sm.table[e];
+    if ((unsigned)s < (unsigned)S)
+      atomicAdd(&cnt_h[s], 1);      // integer counts: the result is order-independent
+    else
+      atomicAdd(&cnt_c[e], 1);
+  }
+  __syncthreads();
+  padded_scan<NT>(cnt_h, cum_h, S, g.bs, warp_h);
+  padded_scan<NT>(cnt_c, cum_c, E, g.bs, warp_c);
+  __syncthreads();
+  if (t == 0) {
+    g.npad_hot[0] = cum_h[S];
+    g.npad_cold[0] = cum_c[E];
+  }
+
+  // ---- block -> bucket ids (the hot side carries slot indices) ---------------------------
+  for (int b = t; b < S; b += NT)
+    for (int i = cum_h[b]; i < cum_h[b + 1]; i += g.bs)
+      if (i / g.bs < g.NB) g.eids_hot[i / g.bs] = b;
+  for (int b = t; b < E; b += NT)
+    for (int i = cum_c[b]; i < cum_c[b + 1]; i += g.bs)
+      if (i / g.bs < g.NB) g.eids_cold[i / g.bs] = b;
+  for (int b = t; b < S; b += NT) cnt_h[b] = cum_h[b];   // counts become cursors
+  for (int b = t; b < E; b += NT) cnt_c[b] = cum_c[b];
+  __syncthreads();
+
+  // ---- placement: one warp walks the tokens in order, so each bucket lists its tokens in
+  // ascending index for every mk (match_any ranks lanes that share a bucket) -------------
+  if (t < 32) {
+    const unsigned below = (1u << lane) - 1u;
+    for (int base = 0; base < mk; base += 32) {
+      const int i = base + lane;
+      int key = -1;
+      if (i < mk) {
+        const int e = a.ids[i];
+        if (e >= 0 && e < E) {
+          const int s = sm.table[e];
+          key = ((unsigned)s < (unsigned)S) ? s : S + e;
+        }
+      }
+      const unsigned same = __match_any_sync(0xffffffffu, key);
+      int* cursor = key < 0 ? nullptr : (key < S ? &cnt_h[key] : &cnt_c[key - S]);
+      const int pos = cursor ? *cursor + __popc(same & below) : 0;
+      __syncwarp();
+      if (cursor && (same & below) == 0) *cursor += __popc(same);
+      __syncwarp();
+      if (cursor && pos < g.L) (key < S ? g.sorted_hot : g.sorted_cold)[pos] = i;
+    }
   }
 }
 
@@ -261,6 +444,7 @@ __global__ void __launch_bounds__(NT) manage_kernel(const __grid_constant__ Mana
 // gather
 
 constexpr int kGatherThreads = 256;
+constexpr int kGatherCtasPerSm = 2;
 constexpr int kGatherUnroll = 8;                                 // 16-byte loads in flight
 constexpr int kTileVecs = kGatherThreads * kGatherUnroll;        // 32 KiB per tile
 
@@ -359,11 +543,27 @@ int launch_manage(const ManageArgs& a, cudaStream_t stream) {
   return (int)cudaLaunchKernelEx(&cfg, manage_kernel<NT>, a);
 }
 
+template <int NT>
+int launch_fused(const ManageArgs& a, const AlignArgs& g, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = fused_smem_bytes(a.E, a.S);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, fused_kernel<NT>, a, g);
+}
+
 int manage_checked(const ManageArgs& a, cudaStream_t stream) {
   if (a.E <= 0 || a.E > EXPERT_CACHE_MAX_EXPERTS) return -1;
   if (a.S <= 0 || a.S > EXPERT_CACHE_MAX_SLOTS || a.S > (1 << kSlotBits) - 1) return -1;
   if (a.max_inserts < 0 || a.max_inserts > EXPERT_CACHE_MAX_INSERTS) return -1;
   if (a.policy < 0 || a.policy > 1) return -1;
+  if (a.S <= 128) return launch_manage<128>(a, stream);
   if (a.S <= 256) return launch_manage<256>(a, stream);
   return launch_manage<1024>(a, stream);
 }
@@ -393,6 +593,9 @@ ManageArgs make_manage_args(const int* topk_ids, int mk, int E, int S, int max_d
   a.out_elem_bytes = 4;
   return a;
 }
+
+// SM count per device, looked up once (sizes the gather grid).
+std::atomic<int> g_sm_count[kMaxDevices];
 
 // Device address of g_noalloc_routed on the current device, looked up once per device.
 std::atomic<void*> g_noalloc_routed_addr[kMaxDevices];
@@ -438,6 +641,34 @@ int expert_cache_manage_remap(const int* topk_ids, int mk, int E, int S, int max
   a.out_ids = mk > 0 ? out_ids : nullptr;   // nothing to remap: behaves as manage
   a.out_elem_bytes = out_elem_bytes;
   return manage_checked(a, stream);
+}
+
+int expert_cache_fused(const int* topk_ids, int mk, int E, int S, int max_distinct,
+                       int max_inserts, int* table, int* map_cold, int* slot_expert,
+                       long long* slot_stamp, unsigned char* routed, long long* step,
+                       int* miss, int* n_miss, int bs, int L, int NB, int* sorted_hot,
+                       int* eids_hot, int* npad_hot, int* sorted_cold, int* eids_cold,
+                       int* npad_cold, cudaStream_t stream) {
+  if (E <= 0 || E > EXPERT_CACHE_FUSED_MAX_EXPERTS || S <= 0 || S > EXPERT_CACHE_MAX_SLOTS)
+    return -1;
+  if (bs <= 0 || L <= 0 || NB <= 0 || mk < 0) return -1;
+  if (max_inserts < 0 || max_inserts > EXPERT_CACHE_MAX_INSERTS) return -1;
+  // The fused path is LRU without ageing, like the reference's (expert_cache.hip:481, 505).
+  const ManageArgs a = make_manage_args(topk_ids, mk, E, S, max_distinct, max_inserts, table,
+                                        map_cold, slot_expert, slot_stamp, routed, step,
+                                        miss, n_miss, 0, 0);
+  AlignArgs g{};
+  g.bs = bs;
+  g.L = L;
+  g.NB = NB;
+  g.sorted_hot = sorted_hot;
+  g.eids_hot = eids_hot;
+  g.npad_hot = npad_hot;
+  g.sorted_cold = sorted_cold;
+  g.eids_cold = eids_cold;
+  g.npad_cold = npad_cold;
+  if (S <= 256) return launch_fused<256>(a, g, stream);
+  return launch_fused<1024>(a, g, stream);
 }
 
 int expert_cache_manage_remap_noalloc(const int* topk_ids, int mk, int E, int S,
@@ -493,9 +724,20 @@ int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void*
   a.miss = miss;
   a.n_miss = n_miss;
 
-  const long long budget = (long long)chunks * (long long)lanes;
+  // chunks * lanes is the CTA budget; more than two CTAs per SM never moved bytes faster
+  // (the host link is the bound), and an idle launch (no misses) retires sooner small.
+  long long grid = (long long)chunks * (long long)lanes;
+  const int dev = current_device();
+  if (dev < 0) return (int)cudaErrorInvalidDevice;
+  int sms = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (sms == 0) {
+    const cudaError_t err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return (int)err;
+    g_sm_count[dev].store(sms, std::memory_order_relaxed);
+  }
+  grid = grid < (long long)kGatherCtasPerSm * sms ? grid : (long long)kGatherCtasPerSm * sms;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)(budget < (1 << 20) ? budget : (1 << 20)));
+  cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kGatherThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
