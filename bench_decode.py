@@ -228,6 +228,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
         env["EXPERT_CACHE_SLOTS"] = str(mode["slots"])
     env["EXPERT_CACHE_POLICY"] = args.policy
     env["EXPERT_CACHE_STATS"] = "1" if args.stats else "0"
+    if args.deterministic:
+        env["VLLM_BATCH_INVARIANT"] = "1"   # vLLM's deterministic (batch-invariant) kernels
     # the counters are fetched with collective_rpc(<function>), which vLLM pickles
     env["VLLM_ALLOW_INSECURE_SERIALIZATION"] = "1"
     log = logdir / f"decode_{mode['name']}.log"
@@ -235,7 +237,9 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
            json.dumps(mode), "--model", str(model_dir), "--tp", str(args.tp),
            "--prompt", str(args.prompt), "--gen", str(args.gen), "--seed", str(args.seed),
            "--batch", str(args.batch), "--vocab", str(MODELS[args.arch][1]),
-           "--gpu-util", str(args.gpu_util)]
+           "--gpu-util", str(args.gpu_util), "--moe-backend", args.moe_backend]
+    if args.no_autotune or args.deterministic:
+        cmd.append("--no-autotune")
     t0 = time.time()
     with open(log, "w") as f:
         rc = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, stderr=f, text=True,
@@ -261,6 +265,10 @@ def child(mode: dict, a) -> None:
               dtype="bfloat16", tensor_parallel_size=a.tp, max_model_len=a.prompt + a.gen + 16,
               gpu_memory_utilization=a.gpu_util, max_num_seqs=a.batch, seed=a.seed,
               enable_prefix_caching=False)
+    if a.moe_backend != "auto":
+        kw["moe_backend"] = a.moe_backend
+    if a.no_autotune:
+        kw["enable_flashinfer_autotune"] = False
     if mode.get("offload"):
         kw.update(cpu_offload_gb=mode["offload_gb"], cpu_offload_params={"experts"})
     t0 = time.time()
@@ -328,6 +336,15 @@ def main(argv=None):
     ap.add_argument("--stats", action="store_true",
                     help="EXPERT_CACHE_STATS=1: count installs (adds one small kernel per "
                          "layer-step, so keep it off for timing)")
+    ap.add_argument("--moe-backend", default="auto",
+                    help="vLLM MoE backend; the cache needs a modular (non-monolithic) one, "
+                         "e.g. 'triton' where vLLM's default would be flashinfer_trtllm")
+    ap.add_argument("--no-autotune", action="store_true",
+                    help="disable FlashInfer's start-up autotuning (a source of run-to-run "
+                         "kernel choice, and slow on host-resident weights)")
+    ap.add_argument("--deterministic", action="store_true",
+                    help="VLLM_BATCH_INVARIANT=1 and no autotuning in every mode, to compare "
+                         "tokens and logprobs without the engine's own run-to-run spread")
     ap.add_argument("--control", action="store_true",
                     help="run the resident mode twice to measure the engine's own spread")
     ap.add_argument("--mode-timeout", type=int, default=1200)
@@ -371,7 +388,8 @@ def main(argv=None):
         r["resident_top2_gap_at_divergence"] = (None if first is None
                                                 else round(base["gaps"][first], 5))
         slim = {k: v for k, v in r.items() if k not in ("tokens", "logprobs", "gaps")}
-        slim.update(arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
+        slim.update(moe_backend=a.moe_backend, deterministic=a.deterministic,
+                    arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
                     prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant)
         print(json.dumps(slim), flush=True)
         results.append(slim)

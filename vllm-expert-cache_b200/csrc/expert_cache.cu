@@ -507,8 +507,8 @@ int current_device() {
 // Opt each manage instantiation into the full shared-memory carve-out once per device.
 template <int NT>
 cudaError_t ensure_manage_smem(int dev) {
-  static bool done[kMaxDevices] = {};
-  if (done[dev]) return cudaSuccess;
+  static std::atomic<bool> done[kMaxDevices];
+  if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
   int optin = 0;
   cudaError_t err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (err != cudaSuccess) return err;
@@ -517,7 +517,7 @@ cudaError_t ensure_manage_smem(int dev) {
   if (err != cudaSuccess) return err;
   err = cudaFuncSetAttribute(manage_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)fa.sharedSizeBytes);
-  if (err == cudaSuccess) done[dev] = true;
+  if (err == cudaSuccess) done[dev].store(true, std::memory_order_release);
   return err;
 }
 
