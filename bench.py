@@ -48,9 +48,9 @@ TOP_K = 8
 L2_BYTES = 126 * 1024 * 1024
 # dram__bytes_read.sum + dram__bytes_write.sum of one gather launch at the default
 # workload (4 misses), from the ncu capture summarised in profiles/gather_kernel_s64_m4.txt:
-# 16,128 B read + 0 B written.  The host-memory reads are not DRAM traffic and the slot
+# 9,728 B read + 0 B written.  The host-memory reads are not DRAM traffic and the slot
 # writes are still in L2 when the launch ends.
-GATHER_DRAM_BYTES = 16128
+GATHER_DRAM_BYTES = 9728
 
 
 def parse(argv=None):

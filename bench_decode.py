@@ -166,10 +166,19 @@ def init_synthetic_weights(model, std: float = 0.02) -> None:
 
 
 def cache_stats_on_worker(worker) -> list:
-    """collective_rpc target: every armed layer's counters (EXPERT_CACHE_STATS=1)."""
+    """collective_rpc target: every armed layer's counters (EXPERT_CACHE_STATS=1), the
+    tensors it mirrors and every name bound to slot storage during a cached step."""
     model = worker.model_runner.get_model()
-    return [m._expert_cache.stats() for m in model.modules()
-            if getattr(m, "_expert_cache", None) is not None]
+    out = []
+    for m in model.modules():
+        c = getattr(m, "_expert_cache", None)
+        if c is not None:
+            st = c.stats()
+            st["mirrored"] = {n: list(c.slots[n].shape) for n in c.names}
+            st["bound"] = sorted(c.bound)
+            st["method"] = type(m.quant_method).__name__
+            out.append(st)
+    return out
 
 
 def register_synthetic_loader() -> None:
@@ -222,6 +231,7 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
     env["PYTHONPATH"] = os.pathsep.join([str(site), str(PKG), str(ROOT),
                                          env.get("PYTHONPATH", "")])
     env["VLLM_PLUGINS"] = "expert_cache,synthetic_w8a8"
+    env.setdefault("VLLM_LOGGING_LEVEL", "INFO")
     env.pop("EXPERT_CACHE_SLOTS", None)
     env["EXPERT_CACHE_DISABLE"] = "0" if mode.get("slots") else "1"
     if mode.get("slots"):
@@ -306,9 +316,13 @@ def child(mode: dict, a) -> None:
         if layers:
             steps = sum(x["steps"] for x in layers)
             installs = sum(x.get("installs", 0) for x in layers)
-            cache = {"armed_layers": len(layers), "layer_steps": steps, "installs": installs,
-                     "installs_per_layer_step": round(installs / max(steps, 1), 4),
-                     "bytes_per_install": layers[0].get("bytes_per_install")}
+            cache = {"armed_layers": len(layers), "layer_steps": steps,
+                     "mirrored": layers[0]["mirrored"], "bound": layers[0]["bound"],
+                     "method": layers[0]["method"]}
+            if "installs" in layers[0]:
+                cache.update(installs=installs,
+                             installs_per_layer_step=round(installs / max(steps, 1), 4),
+                             bytes_per_install=layers[0].get("bytes_per_install"))
     out = {"mode": mode["name"], "slots": mode.get("slots"), "offload": bool(mode.get("offload")),
            "tp": a.tp, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
            "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
