@@ -232,6 +232,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
                                          env.get("PYTHONPATH", "")])
     env["VLLM_PLUGINS"] = "expert_cache,synthetic_w8a8"
     env.setdefault("VLLM_LOGGING_LEVEL", "INFO")
+    if args.debug_calls:
+        env["EXPERT_CACHE_DEBUG"] = str(args.debug_calls)
     env.pop("EXPERT_CACHE_SLOTS", None)
     env["EXPERT_CACHE_DISABLE"] = "0" if mode.get("slots") else "1"
     if mode.get("slots"):
@@ -254,6 +256,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
     with open(log, "w") as f:
         rc = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, stderr=f, text=True,
                             timeout=args.mode_timeout)
+    with open(log, "a") as f:            # vLLM's loggers (and ours) write to stdout
+        f.write(rc.stdout)
     res = None
     for line in rc.stdout.splitlines():
         if line.startswith("{\"decode_result\""):
@@ -359,6 +363,8 @@ def main(argv=None):
     ap.add_argument("--deterministic", action="store_true",
                     help="VLLM_BATCH_INVARIANT=1 and no autotuning in every mode, to compare "
                          "tokens and logprobs without the engine's own run-to-run spread")
+    ap.add_argument("--debug-calls", type=int, default=0,
+                    help="EXPERT_CACHE_DEBUG: log the first N MoE calls per armed layer")
     ap.add_argument("--control", action="store_true",
                     help="run the resident mode twice to measure the engine's own spread")
     ap.add_argument("--mode-timeout", type=int, default=1200)
@@ -401,7 +407,8 @@ def main(argv=None):
         # at a divergence: how close the resident run's own top-2 were (a near-tie flip)
         r["resident_top2_gap_at_divergence"] = (None if first is None
                                                 else round(base["gaps"][first], 5))
-        slim = {k: v for k, v in r.items() if k not in ("tokens", "logprobs", "gaps")}
+        slim = {k: v for k, v in r.items() if k not in ("logprobs", "gaps")}
+        slim["tokens"] = r["tokens"][:16]
         slim.update(moe_backend=a.moe_backend, deterministic=a.deterministic,
                     arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
                     prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant)

@@ -186,10 +186,16 @@ def arm(layer, method, logger) -> bool:
             return False
 
     stock_apply = method.apply
+    debug_left = [settings.debug_calls]
 
     # vLLM calls apply by keyword: these parameter names are part of the contract.
     def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
               shared_experts_input=None):
+        if debug_left[0] > 0:
+            debug_left[0] -= 1
+            logger.warning("expert-cache debug: %s topk_ids %s %s -> %s", kind,
+                           tuple(topk_ids.shape), topk_ids.dtype,
+                           "cached" if cache.fits(topk_ids) else "read-through")
         if not cache.fits(topk_ids):
             return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
                                shared_experts_input)

@@ -11,6 +11,9 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
   EXPERT_CACHE_LIB        -       explicit path of libexpertcache.so
   EXPERT_CACHE_CHUNKS     16      gather CTA budget = CHUNKS * LANES
   EXPERT_CACHE_LANES      64
+  EXPERT_CACHE_DEBUG      0       N > 0 logs the first N MoE calls of each armed layer
+                                  (routing shape and cached / read-through path); new,
+                                  off by default
   EXPERT_CACHE_STATS      0       '1' keeps a device-side running total of installs per
                                   layer (one extra tiny kernel per cached step; new in
                                   this build, off by default)
@@ -62,6 +65,10 @@ class Settings:
     @property
     def lanes(self) -> int:
         return int(_env("EXPERT_CACHE_LANES", "64"))
+
+    @property
+    def debug_calls(self) -> int:
+        return int(_env("EXPERT_CACHE_DEBUG", "0") or 0)
 
     @property
     def stats(self) -> bool:
