@@ -249,7 +249,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
            json.dumps(mode), "--model", str(model_dir), "--tp", str(args.tp),
            "--prompt", str(args.prompt), "--gen", str(args.gen), "--seed", str(args.seed),
            "--batch", str(args.batch), "--vocab", str(MODELS[args.arch][1]),
-           "--gpu-util", str(args.gpu_util), "--moe-backend", args.moe_backend]
+           "--gpu-util", str(args.gpu_util), "--moe-backend", args.moe_backend,
+           "--temperature", str(args.temperature)]
     if args.no_autotune or args.deterministic:
         cmd.append("--no-autotune")
     t0 = time.time()
@@ -292,7 +293,11 @@ def child(mode: dict, a) -> None:
     prompts = [{"prompt_token_ids": rng.integers(0, a.vocab, size=a.prompt).tolist()}
                for _ in range(a.batch)]
     greedy = dict(temperature=0.0, ignore_eos=True, detokenize=False)
-    llm.generate(prompts, SamplingParams(max_tokens=32, **greedy), use_tqdm=False)  # warm
+    # timed runs: greedy, or seeded sampling so the input token changes every step (a
+    # random-init model's greedy output repeats one token, which makes routing repeat)
+    timed = greedy if a.temperature == 0 else dict(
+        temperature=a.temperature, seed=a.seed, ignore_eos=True, detokenize=False)
+    llm.generate(prompts, SamplingParams(max_tokens=32, **timed), use_tqdm=False)  # warm
     ref = llm.generate(prompts[:1], SamplingParams(max_tokens=a.gen, logprobs=2, **greedy),
                        use_tqdm=False)[0].outputs[0]
     tokens = list(ref.token_ids)
@@ -307,7 +312,7 @@ def child(mode: dict, a) -> None:
         best = None
         for _ in range(2):
             t = time.perf_counter()
-            llm.generate(prompts, SamplingParams(max_tokens=n, **greedy), use_tqdm=False)
+            llm.generate(prompts, SamplingParams(max_tokens=n, **timed), use_tqdm=False)
             dt = time.perf_counter() - t
             best = dt if best is None else min(best, dt)
         times[n] = best
@@ -363,6 +368,9 @@ def main(argv=None):
     ap.add_argument("--deterministic", action="store_true",
                     help="VLLM_BATCH_INVARIANT=1 and no autotuning in every mode, to compare "
                          "tokens and logprobs without the engine's own run-to-run spread")
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="timed runs only: 0 = greedy; > 0 = seeded sampling (the parity "
+                         "run stays greedy)")
     ap.add_argument("--debug-calls", type=int, default=0,
                     help="EXPERT_CACHE_DEBUG: log the first N MoE calls per armed layer")
     ap.add_argument("--control", action="store_true",
@@ -410,6 +418,7 @@ def main(argv=None):
         slim = {k: v for k, v in r.items() if k not in ("logprobs", "gaps")}
         slim["tokens"] = r["tokens"][:16]
         slim.update(moe_backend=a.moe_backend, deterministic=a.deterministic,
+                    temperature=a.temperature,
                     arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
                     prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant)
         print(json.dumps(slim), flush=True)
