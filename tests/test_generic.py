@@ -296,3 +296,17 @@ def test_unrecognised_weight_names_are_reported():
     layer.register_parameter("w13_qweight_x", layer._parameters.pop("w13_weight"))
     ok, log = arm(layer, QuantMethod.__new__(QuantMethod))
     assert not ok and log.said("no recognised expert weight pair")
+
+
+def test_debug_trace_logs_the_path(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_DEBUG", "2")
+    layer = RoutedExperts()
+    m = QuantMethod(layer)
+    ok, log = arm(layer, m)
+    assert ok
+    layer._expert_cache.refresh = lambda ids: ids.clone()
+    for n in (2, S + 1, 2):
+        m.apply(layer, torch.randn(1, H), torch.ones(1, n), torch.zeros(1, n, dtype=torch.int32))
+    traced = [x for x in log.msgs if "expert-cache debug" in x]
+    assert len(traced) == 2                  # only the first N calls
+    assert traced[0].endswith("-> cached") and traced[1].endswith("-> read-through")
