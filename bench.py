@@ -447,18 +447,35 @@ def cpu_baseline_port(layer, trace, steps):
     return moved / dt / 1e9, dt
 
 
-def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64):
+def reference_timing_trace(steps=4096, E=512, rows=5, k=10, s=1.1, seed=0):
+    """The reference's manage timing shape (tests/test_policy.py:312-324): one decode step
+    of 5 rows x top-10 drawn from Zipf(1.1) over 512 experts, repeated every call, so
+    after the first call the kernel runs its steady state of 50 routings, all hits."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    p = np.arange(1, E + 1, dtype=float) ** -s
+    p /= p.sum()
+    one = np.concatenate([rng.choice(E, k, replace=False, p=p) for _ in range(rows)])
+    return np.tile(one.astype(np.int32), (steps, 1))
+
+
+def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64, E=E_EXPERTS, trace=None,
+               max_distinct=None, max_inserts=None):
     """BASELINE config 1 on the GPU: the 4096-step sticky-Zipf trace through the manage
     kernel from a cold cache, captured as one CUDA graph of 4096 manage+remap nodes (as
     vLLM replays them).  Returns device us per layer-step, the graph-node floor (a graph
-    of as many empty kernels), the miss total and the final state."""
+    of as many empty kernels), the miss total and the final state.  ``trace`` /
+    ``E`` / ``S`` / the caps select another workload (the reference's timing shape)."""
     import torch
     from vllm_expert_cache import _lib
     from vllm_expert_cache.synthetic import sticky_zipf_trace
     h = _lib.lib()
-    E = E_EXPERTS
-    trace = sticky_zipf_trace(seed, steps=steps)
+    if trace is None:
+        trace = sticky_zipf_trace(seed, steps=steps, E=E)
+    steps = trace.shape[0]
     mk = trace.shape[1]
+    md = min(E, mk) if max_distinct is None else max_distinct
+    mi = S if max_inserts is None else max_inserts
     i32, i64 = torch.int32, torch.int64
     st = {"table": torch.full((E,), -1, dtype=i32, device=dev),
           "map_cold": torch.arange(E, dtype=i32, device=dev),
@@ -466,7 +483,7 @@ def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64):
           "slot_stamp": torch.zeros((S,), dtype=i64, device=dev),
           "routed": torch.zeros((E,), dtype=torch.uint8, device=dev),
           "step": torch.zeros((1,), dtype=i64, device=dev),
-          "miss": torch.zeros((2 * S,), dtype=i32, device=dev),
+          "miss": torch.zeros((2 * max(S, mi),), dtype=i32, device=dev),
           "n_miss": torch.zeros((1,), dtype=i32, device=dev)}
     init = {k: v.clone() for k, v in st.items()}
     P = ctypes.c_void_p
@@ -477,7 +494,7 @@ def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64):
     nm_hist = torch.zeros(steps, dtype=i32, device=dev)
 
     def launch(t, stream):
-        rc = h.expert_cache_manage_remap(P(ids[t].data_ptr()), mk, E, S, min(E, mk), S, *sp,
+        rc = h.expert_cache_manage_remap(P(ids[t].data_ptr()), mk, E, S, md, mi, *sp,
                                          policy_code, decay, P(out[t].data_ptr()), 4, stream)
         if rc:
             raise RuntimeError(f"expert_cache_manage_remap rc={rc}")
@@ -534,14 +551,17 @@ def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64):
             "misses": misses, "lookups": int(steps * mk)}, trace, final, nm_hist.cpu().numpy()
 
 
-def policy_sim_cpu_baseline(trace, policy_code, decay, final, nm_gpu, S=64):
+def policy_sim_cpu_baseline(trace, policy_code, decay, final, nm_gpu, S=64, E=E_EXPERTS,
+                            max_distinct=None, max_inserts=None):
     """The same trace through the C oracle on one core: its time per step, and the check
     that the GPU's final state and per-step miss counts are the oracle's."""
     import numpy as np
     from oracle import policy, policy_c
-    st = policy.CacheState(E_EXPERTS, S)
+    md = min(E, trace.shape[1]) if max_distinct is None else max_distinct
+    mi = S if max_inserts is None else max_inserts
+    st = policy.CacheState(E, S, miss_cap=max(S, mi))
     t0 = time.perf_counter()
-    nm = policy_c.run(st, trace, min(E_EXPERTS, trace.shape[1]), S, policy_code, decay)
+    nm = policy_c.run(st, trace, md, mi, policy_code, decay)
     dt = time.perf_counter() - t0
     same = bool(np.array_equal(nm, nm_gpu)) and all(
         np.array_equal(final[k].numpy(), getattr(st, k)) for k in final)
@@ -637,6 +657,17 @@ def run_ours(a, dist):
                     res.update(policy_sim_cpu_baseline(tr, code, a.decay, fin, nm))
                 sim[name] = res
             line["policy_sim"] = sim
+            # the reference's own manage timing shape (E512 S257, 50 routings per call,
+            # max_distinct 128, max_inserts 64; ~11.3 us per call on its MI210)
+            tr = reference_timing_trace()
+            res, tr, fin, nm = policy_sim(dev, 1, a.decay, S=257, E=512, trace=tr,
+                                          max_distinct=128, max_inserts=64)
+            if dist.rank == 0 and dist.world == 1 and not a.no_cpu:
+                res.update(policy_sim_cpu_baseline(tr, 1, a.decay, fin, nm, S=257, E=512,
+                                                   max_distinct=128, max_inserts=64))
+            res["workload"] = ("E512 S257, 5 rows x top-10 Zipf(1.1) repeated (steady "
+                               "state, all hits after the first call), LFU")
+            line["manage_reference_shape"] = res
         if not a.sweep and not a.no_cpu and dist.rank == 0 and dist.world == 1:
             n = min(K, 200)
             gbs, dt = cpu_baseline_port(layer, trace[W:], n)
