@@ -25,6 +25,7 @@ resident, max |logprob difference| of the chosen tokens) and a summary line.
     python bench_decode.py [--arch qwen3-30b-a3b] [--quant int8-experts] [--tp 1]
                            [--slots 16 32 64 96] [--gen 512] [--batch 1]
     python bench_decode.py --arch mixtral-8x7b --quant bf16 --slots 2 4 6 --gen 64
+    python bench_decode.py --batch 8 --slots 32 --split-wide 0 4 --parity-batch ...
 """
 
 from __future__ import annotations
@@ -240,6 +241,9 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
         env["EXPERT_CACHE_SLOTS"] = str(mode["slots"])
     env["EXPERT_CACHE_POLICY"] = args.policy
     env["EXPERT_CACHE_STATS"] = "1" if args.stats else "0"
+    env.pop("EXPERT_CACHE_SPLIT_WIDE", None)
+    if mode.get("split"):
+        env["EXPERT_CACHE_SPLIT_WIDE"] = str(mode["split"])
     if args.deterministic:
         env["VLLM_BATCH_INVARIANT"] = "1"   # vLLM's deterministic (batch-invariant) kernels
     # the counters are fetched with collective_rpc(<function>), which vLLM pickles
@@ -251,6 +255,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
            "--batch", str(args.batch), "--vocab", str(MODELS[args.arch][1]),
            "--gpu-util", str(args.gpu_util), "--moe-backend", args.moe_backend,
            "--temperature", str(args.temperature)]
+    if args.parity_batch:
+        cmd.append("--parity-batch")
     if args.no_autotune or args.deterministic:
         cmd.append("--no-autotune")
     t0 = time.time()
@@ -298,15 +304,19 @@ def child(mode: dict, a) -> None:
     timed = greedy if a.temperature == 0 else dict(
         temperature=a.temperature, seed=a.seed, ignore_eos=True, detokenize=False)
     llm.generate(prompts, SamplingParams(max_tokens=32, **timed), use_tqdm=False)  # warm
-    ref = llm.generate(prompts[:1], SamplingParams(max_tokens=a.gen, logprobs=2, **greedy),
-                       use_tqdm=False)[0].outputs[0]
-    tokens = list(ref.token_ids)
-    lps = [float(d[t].logprob) for d, t in zip(ref.logprobs, tokens)]
-    # top-1 minus top-2 logprob per position: how close each greedy choice was to a tie
-    gaps = []
-    for d in ref.logprobs:
-        v = sorted((float(x.logprob) for x in d.values()), reverse=True)
-        gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
+    # parity run: the first prompt alone, or (--parity-batch) the whole batch so that its
+    # decode steps have the timed runs' width; sequences are concatenated in prompt order
+    refs = llm.generate(prompts if a.parity_batch else prompts[:1],
+                        SamplingParams(max_tokens=a.gen, logprobs=2, **greedy), use_tqdm=False)
+    tokens, lps, gaps = [], [], []
+    for r in refs:
+        ref = r.outputs[0]
+        tokens += list(ref.token_ids)
+        lps += [float(d[t].logprob) for d, t in zip(ref.logprobs, ref.token_ids)]
+        # top-1 minus top-2 logprob per position: how close each greedy choice was to a tie
+        for d in ref.logprobs:
+            v = sorted((float(x.logprob) for x in d.values()), reverse=True)
+            gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
     times = {}
     for n in (1, a.gen):
         best = None
@@ -332,7 +342,8 @@ def child(mode: dict, a) -> None:
                 cache.update(installs=installs,
                              installs_per_layer_step=round(installs / max(steps, 1), 4),
                              bytes_per_install=layers[0].get("bytes_per_install"))
-    out = {"mode": mode["name"], "slots": mode.get("slots"), "offload": bool(mode.get("offload")),
+    out = {"mode": mode["name"], "slots": mode.get("slots"), "split_wide": mode.get("split", 0),
+           "offload": bool(mode.get("offload")),
            "tp": a.tp, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
            "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
            "cache": cache, "tokens": tokens, "logprobs": lps, "gaps": gaps}
@@ -375,6 +386,11 @@ def main(argv=None):
                     help="EXPERT_CACHE_DEBUG: log the first N MoE calls per armed layer")
     ap.add_argument("--control", action="store_true",
                     help="run the resident mode twice to measure the engine's own spread")
+    ap.add_argument("--split-wide", type=int, nargs="*", default=[],
+                    help="EXPERT_CACHE_SPLIT_WIDE values: every slot count runs once per "
+                         "value (0 = the reference's read-through of wide steps)")
+    ap.add_argument("--parity-batch", action="store_true",
+                    help="greedy parity run over the whole batch instead of its first prompt")
     ap.add_argument("--mode-timeout", type=int, default=1200)
     ap.add_argument("--logdir", default="gpurun_out")
     ap.add_argument("--child", default=None)
@@ -394,8 +410,9 @@ def main(argv=None):
         modes.append({"name": "resident-again"})   # the engine's own run-to-run spread
     if not a.no_offload_baseline:
         modes.append({"name": "offload", "offload": True, "offload_gb": a.offload_gb})
-    modes += [{"name": f"slots{s}", "slots": s, "offload": True, "offload_gb": a.offload_gb}
-              for s in a.slots]
+    modes += [{"name": f"slots{s}" + (f"-split{v}" if v else ""), "slots": s, "split": v,
+               "offload": True, "offload_gb": a.offload_gb}
+              for s in a.slots for v in (a.split_wide or [0])]
     results = []
     base = None
     for m in modes:
@@ -420,7 +437,8 @@ def main(argv=None):
         slim.update(moe_backend=a.moe_backend, deterministic=a.deterministic,
                     temperature=a.temperature,
                     arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
-                    prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant)
+                    prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant,
+                    parity_batch=a.parity_batch)
         print(json.dumps(slim), flush=True)
         results.append(slim)
     # the chosen tokens' logprobs within 1e-2 of the resident run's at every position the

@@ -310,3 +310,138 @@ def test_debug_trace_logs_the_path(monkeypatch):
     traced = [x for x in log.msgs if "expert-cache debug" in x]
     assert len(traced) == 2                  # only the first N calls
     assert traced[0].endswith("-> cached") and traced[1].endswith("-> read-through")
+
+
+# --- opt-in split of wide steps (EXPERT_CACHE_SPLIT_WIDE) ---------------------------------
+
+@dataclass
+class ActDesc(Desc):
+    dtype: object = None
+    shape: object = None
+
+
+class Shape:
+    def __init__(self, row, col):
+        self.row, self.col = row, col
+
+
+class RowMethod(QuantMethod):
+    """Per-token stand-in: row i of the output is x[i] + sum(topk_ids[i]) (in slot space
+    on the cached path), so chunk order and chunk contents are both visible."""
+
+    def __init__(self, layer, a1=None, a2=None, result=None):
+        self.a1, self.a2, self.result = a1 or Desc(), a2 or Desc(), result
+        super().__init__(layer)
+        self.calls = []
+
+    def _cfg(self, layer):
+        cfg = super()._cfg(layer)
+        cfg._a1, cfg._a2 = self.a1, self.a2
+        return cfg
+
+    def apply(self, layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        self.calls.append((tuple(topk_ids.shape), layer.global_num_experts))
+        if self.result is not None:
+            return self.result
+        return x + topk_ids.sum(dim=1, keepdim=True).to(x.dtype)
+
+
+def armed_rows(monkeypatch, split, **kw):
+    monkeypatch.setenv("EXPERT_CACHE_SPLIT_WIDE", str(split))
+    layer = RoutedExperts()
+    m = RowMethod(layer, **kw)
+    ok, log = arm(layer, m)
+    assert ok, log.msgs
+    refreshed = []
+
+    def refresh(ids):
+        refreshed.append(ids.clone())
+        return ids + 100
+    layer._expert_cache.refresh = refresh
+    return layer, m, log, refreshed
+
+
+def wide_step(tokens, k=2):
+    x = torch.arange(tokens * H, dtype=torch.float32).reshape(tokens, H)
+    ids = torch.arange(tokens * k, dtype=torch.int32).reshape(tokens, k) % E
+    return x, torch.ones(tokens, k), ids
+
+
+def test_split_is_off_by_default(monkeypatch):
+    layer, m, _, refreshed = armed_rows(monkeypatch, 0)
+    x, w, ids = wide_step(3)                     # 6 ids > S = 4
+    out = m.apply(layer, x, w, ids)
+    assert refreshed == [] and m.calls == [((3, 2), E)]
+    assert torch.equal(out, x + ids.sum(1, keepdim=True))
+
+
+def test_wide_step_is_served_in_cached_chunks(monkeypatch):
+    layer, m, _, refreshed = armed_rows(monkeypatch, 4)
+    x, w, ids = wide_step(5)                     # S // k = 2 tokens a chunk -> 3 chunks
+    out = m.apply(layer, x, w, ids)
+    assert [tuple(r.shape) for r in refreshed] == [(2, 2), (2, 2), (1, 2)]
+    assert torch.equal(torch.cat(refreshed), ids)           # consecutive, in order
+    assert m.calls == [((2, 2), S)] * 2 + [((1, 2), S)]     # every chunk slot-bound
+    assert torch.equal(out, x + (ids + 100).sum(1, keepdim=True))
+    assert layer.global_num_experts == E
+    assert layer.w13_weight.size(0) == E
+
+
+def test_split_limit_reads_through(monkeypatch):
+    layer, m, _, refreshed = armed_rows(monkeypatch, 2)
+    x, w, ids = wide_step(5)                     # needs 3 chunks, limit 2
+    m.apply(layer, x, w, ids)
+    assert refreshed == [] and m.calls == [((5, 2), E)]
+
+
+def test_split_needs_room_for_one_token(monkeypatch):
+    layer, m, _, refreshed = armed_rows(monkeypatch, 8)
+    x, w, ids = wide_step(1, k=S + 1)            # one token already wider than the slots
+    m.apply(layer, x, w, ids)
+    assert refreshed == [] and m.calls == [((1, S + 1), E)]
+
+
+def test_split_skips_steps_with_shared_experts(monkeypatch):
+    layer, m, _, refreshed = armed_rows(monkeypatch, 4)
+    x, w, ids = wide_step(3)
+    m.apply(layer, x, w, ids, shared_experts=object(), shared_experts_input=x)
+    assert refreshed == [] and m.calls == [((3, 2), E)]
+
+
+@pytest.mark.parametrize("a1,a2,splits", [
+    (ActDesc(dtype=torch.int8, shape=Shape(1, -1)), None, True),        # per token
+    (ActDesc(dtype=torch.int8, shape=Shape(1, 128)), None, True),       # per token group
+    (ActDesc(dtype=torch.int8, shape=Shape(128, 128)), None, True),     # K-blocked
+    (ActDesc(dtype="mxfp8", shape=None), None, True),                   # micro-scaled
+    (ActDesc(dtype=torch.int8, shape=Shape(-1, -1), scale=torch.ones(1)), None, True),
+    (ActDesc(dtype=torch.int8, shape=Shape(-1, -1)), None, False),      # dynamic tensor
+    (None, ActDesc(dtype=torch.int8, shape=Shape(-1, -1)), False),
+    (ActDesc(dtype=torch.int8, shape=None), None, False),
+])
+def test_split_requires_token_local_activation_quant(monkeypatch, a1, a2, splits):
+    layer, m, log, refreshed = armed_rows(monkeypatch, 4, a1=a1, a2=a2)
+    x, w, ids = wide_step(3)
+    m.apply(layer, x, w, ids)
+    assert bool(refreshed) == splits
+    assert log.said("not splitting wide steps") == (not splits)
+
+
+def test_split_falls_back_when_apply_returns_a_pair(monkeypatch):
+    layer, m, log, refreshed = armed_rows(monkeypatch, 4,
+                                          result=(torch.zeros(1), torch.zeros(1)))
+    x, w, ids = wide_step(3)
+    out = m.apply(layer, x, w, ids)
+    assert isinstance(out, tuple) and log.said("read through from now on")
+    assert m.calls[-1] == ((3, 2), E)
+    n = len(refreshed)
+    m.apply(layer, x, w, ids)                    # splitting stays off for this layer
+    assert len(refreshed) == n and m.calls[-1] == ((3, 2), E)
+
+
+def test_debug_trace_names_the_split(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_DEBUG", "1")
+    layer, m, log, _ = armed_rows(monkeypatch, 4)
+    x, w, ids = wide_step(5)
+    m.apply(layer, x, w, ids)
+    assert [x for x in log.msgs if "expert-cache debug" in x][0].endswith("-> split 3")

@@ -92,3 +92,26 @@ def test_install_rebinds_hook_and_arms_layers(monkeypatch):
     finally:
         vllm_loader.process_weights_after_loading = stock
         base_loader.process_weights_after_loading = stock
+
+
+def _cfgs():
+    """vLLM's own quant-config factories, with whether a token of the config computes
+    independently of the rest of its step."""
+    from vllm.model_executor.layers.fused_moe import config as c
+    w = torch.ones(4, 8, 1)
+    yield "unquantized", c.FUSED_MOE_UNQUANTIZED_CONFIG, True
+    yield "int8 per-token dynamic", c.int8_w8a8_moe_quant_config(
+        w, w, None, None, per_act_token_quant=True), True
+    yield "int8 per-tensor dynamic", c.int8_w8a8_moe_quant_config(w, w, None, None), False
+    yield "int8 per-tensor static", c.int8_w8a8_moe_quant_config(
+        w, w, torch.ones(1), torch.ones(1)), True
+    yield "fp8 block", c.fp8_w8a8_moe_quant_config(w, w, block_shape=[128, 128]), True
+    yield "fp8 per-tensor dynamic", c.fp8_w8a8_moe_quant_config(w, w), False
+    yield "int4 weight-only", c.int4_w4a16_moe_quant_config(w, w, None, None), True
+
+
+@pytest.mark.parametrize("name,cfg,local", list(_cfgs()), ids=lambda v: v
+                         if isinstance(v, str) else "")
+def test_token_locality_of_vllm_quant_configs(name, cfg, local):
+    from vllm_expert_cache.backends import generic
+    assert (generic._token_local(cfg) is None) == local, name

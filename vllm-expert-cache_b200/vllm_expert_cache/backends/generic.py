@@ -14,7 +14,8 @@ slot binding to get a slot-bound config, refuses the layer if any per-expert ten
 stayed on full [E] storage, and wraps ``method.apply`` on the instance.  A cached step
 swaps the slot buffers, the slot-bound config and ``global_num_experts = S`` in around the
 original ``apply`` and restores everything afterwards; a step wider than the slots calls
-the original untouched.  The hook is vLLM's single post-load call site,
+the original untouched (or, opted in with EXPERT_CACHE_SPLIT_WIDE, runs as a few cached
+steps over consecutive token chunks).  The hook is vLLM's single post-load call site,
 ``model_loader.utils.process_weights_after_loading``, rebound wherever it was imported by
 name.  Refusals are logged and leave the layer on the stock path.
 """
@@ -35,6 +36,8 @@ _QUANT_DESCS = ("_a1", "_a2", "_w1", "_w2")
 _QUANT_FIELDS = ("scale", "alpha_or_gscale", "zp", "bias")
 # Registered names of the two expert weight matrices, plain and packed spellings.
 _WEIGHT_PAIRS = (("w13_weight", "w2_weight"), ("w13_weight_packed", "w2_weight_packed"))
+# Activation quant dtypes whose scales are per block of one row (vLLM's string dtypes).
+_MICRO_SCALED = frozenset({"nvfp4", "mxfp4", "mxfp6_e3m2", "mxfp6_e2m3", "mxfp8"})
 
 _installed = False
 
@@ -88,6 +91,35 @@ def _leaked_full_tensors(cfg, num_experts: int) -> list[str]:
             if isinstance(t, torch.Tensor) and t.dim() >= 1 and t.size(0) == num_experts:
                 leaked.append(f"{dname}.{field}{tuple(t.shape)}")
     return leaked
+
+
+def _token_local(cfg) -> str | None:
+    """Why a token of this quant config does not compute independently of the others in
+    its step, or None when it does.
+
+    The one coupling in a FusedMoEQuantConfig is a dynamic per-tensor activation scale:
+    ``_a1`` / ``_a2`` with a quant dtype, no static scale, and the PER_TENSOR group shape
+    (or none).  Serving such a step in chunks would quantise each chunk against its own
+    maximum.  Token-local are: per-token shapes, K-blocked shapes (vLLM records a block
+    quantiser's activation shape as the weight block, e.g. (128, 128), and quantises per
+    token group), static scales, and the micro-scaled formats, whose scales cover 16 or 32
+    elements of one row (vllm/model_executor/layers/fused_moe/config.py:69-97, 488-560).
+    """
+    if cfg is None:
+        return None
+    for dname in ("_a1", "_a2"):
+        desc = getattr(cfg, dname, None)
+        dtype = getattr(desc, "dtype", None)
+        if dtype is None or dtype in _MICRO_SCALED:
+            continue
+        if getattr(desc, "scale", None) is not None:
+            continue                                  # static scale
+        shape = getattr(desc, "shape", None)
+        if shape is not None and (getattr(shape, "row", -1), getattr(shape, "col", -1)) \
+                != (-1, -1):
+            continue                                  # per token / per token group
+        return f"{dname} is quantised with a dynamic per-tensor scale"
+    return None
 
 
 @contextlib.contextmanager
@@ -187,18 +219,15 @@ def arm(layer, method, logger) -> bool:
 
     stock_apply = method.apply
     debug_left = [settings.debug_calls]
+    split_max = settings.split_wide
+    if split_max:
+        why = _token_local(slot_cfg)
+        if why is not None:
+            logger.info("expert-cache: not splitting wide steps of %s -- %s", kind, why)
+            split_max = 0
+    split = [split_max]
 
-    # vLLM calls apply by keyword: these parameter names are part of the contract.
-    def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
-              shared_experts_input=None):
-        if debug_left[0] > 0:
-            debug_left[0] -= 1
-            logger.warning("expert-cache debug: %s topk_ids %s %s -> %s", kind,
-                           tuple(topk_ids.shape), topk_ids.dtype,
-                           "cached" if cache.fits(topk_ids) else "read-through")
-        if not cache.fits(topk_ids):
-            return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
-                               shared_experts_input)
+    def cached(layer, x, topk_weights, topk_ids, shared_experts, shared_experts_input):
         slot_ids = cache.refresh(topk_ids)
         experts = method.moe_kernel.fused_experts
         saved = (experts.quant_config, method.moe_quant_config, layer.global_num_experts)
@@ -211,6 +240,49 @@ def arm(layer, method, logger) -> bool:
                                    shared_experts_input)
         finally:
             experts.quant_config, method.moe_quant_config, layer.global_num_experts = saved
+
+    def chunk_tokens(x, topk_ids, shared_experts) -> int:
+        """Tokens per chunk when this wide step may be split, else 0 (read through)."""
+        if not split[0] or shared_experts is not None or topk_ids.dim() != 2:
+            return 0
+        if not isinstance(x, torch.Tensor) or x.size(0) != topk_ids.size(0):
+            return 0
+        per = cache.S // max(1, topk_ids.size(1))
+        if per < 1 or -(-topk_ids.size(0) // per) > split[0]:
+            return 0
+        return per
+
+    # vLLM calls apply by keyword: these parameter names are part of the contract.
+    def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        fits = cache.fits(topk_ids)
+        per = 0 if fits else chunk_tokens(x, topk_ids, shared_experts)
+        if debug_left[0] > 0:
+            debug_left[0] -= 1
+            path = ("cached" if fits else
+                    f"split {-(-topk_ids.size(0) // per)}" if per else "read-through")
+            logger.warning("expert-cache debug: %s topk_ids %s %s -> %s", kind,
+                           tuple(topk_ids.shape), topk_ids.dtype, path)
+        if fits:
+            return cached(layer, x, topk_weights, topk_ids, shared_experts,
+                          shared_experts_input)
+        if not per:
+            return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
+                               shared_experts_input)
+        # Each chunk is an ordinary cached step over consecutive tokens; a token's output
+        # depends only on its own row (checked by _token_local at arm time).
+        outs = []
+        for lo in range(0, topk_ids.size(0), per):
+            out = cached(layer, x[lo:lo + per], topk_weights[lo:lo + per],
+                         topk_ids[lo:lo + per], None, None)
+            if not isinstance(out, torch.Tensor):
+                logger.warning("expert-cache: %s apply returned %s, not a tensor; wide "
+                               "steps read through from now on", kind, type(out).__name__)
+                split[0] = 0
+                return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
+                                   shared_experts_input)
+            outs.append(out)
+        return torch.cat(outs, dim=0)
 
     method.apply = apply
     layer._expert_cache = cache

@@ -17,6 +17,10 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
   EXPERT_CACHE_STATS      0       '1' keeps a device-side running total of installs per
                                   layer (one extra tiny kernel per cached step; new in
                                   this build, off by default)
+  EXPERT_CACHE_SPLIT_WIDE 0       N > 0 serves a step wider than the slots as up to N
+                                  cached chunks of S // top_k tokens when the layer's
+                                  activation quantisation is per token (new, off by
+                                  default: 0 keeps the reference's read-through)
 
 ``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
 """
@@ -73,6 +77,10 @@ class Settings:
     @property
     def stats(self) -> bool:
         return _env("EXPERT_CACHE_STATS", "0") == "1"
+
+    @property
+    def split_wide(self) -> int:
+        return max(0, int(_env("EXPERT_CACHE_SPLIT_WIDE", "0") or 0))
 
     def slots_for(self, num_experts: int) -> int:
         want = self.slots
