@@ -76,6 +76,33 @@ EXPERT_CACHE_API int expert_cache_manage_remap(const int* topk_ids, int mk, int 
                               int* miss, int* n_miss, int policy, int decay, void* out_ids,
                               int out_elem_bytes, cudaStream_t stream);
 
+/* expert_cache_manage for an expert-parallel layer, where this rank holds E of the
+ * E_global experts.
+ *
+ * topk_ids are global expert ids. Each is translated on load through
+ * expert_map [E_global] (int32: global id -> local expert in [0, E), or -1 for another
+ * rank's expert) before the policy sees it. Ids outside [0, E_global) and map entries
+ * outside [0, E) count as padding. The policy step is then expert_cache_manage's on the
+ * local ids.
+ *
+ * In the same launch the updated table is composed with the map:
+ *   out_map[g] = expert_map[g] in [0, E) ? table[expert_map[g]] : -1   (int32, E_global)
+ * This is a global id -> slot map for a kernel that takes an expert map (vLLM's fused
+ * MoE with expert_map). The routing ids themselves are left untouched.
+ *
+ * Returns -1 on the manage rules above, or when expert_map or out_map is NULL, or when
+ * E_global <= 0.
+ *
+ * Has no counterpart in the reference: the reference refuses expert-parallel layers
+ * (vllm_expert_cache/backends/generic.py:145-149). It composes the reference's manage
+ * step (kernels/expert_cache.hip:191-282) with vLLM's expert map
+ * (vllm/model_executor/layers/fused_moe/expert_map_manager.py:22-113). */
+EXPERT_CACHE_API int expert_cache_manage_ep(
+    const int* topk_ids, int mk, const int* expert_map, int E_global, int E, int S,
+    int max_distinct, int max_inserts, int* table, int* map_cold, int* slot_expert,
+    long long* slot_stamp, unsigned char* routed, long long* step, int* miss, int* n_miss,
+    int policy, int decay, int* out_map, cudaStream_t stream);
+
 /* Largest expert count of expert_cache_fused (reference expert_cache.hip:341, MAXE). */
 #define EXPERT_CACHE_FUSED_MAX_EXPERTS 1024
 

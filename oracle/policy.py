@@ -169,6 +169,39 @@ def remap(table: np.ndarray, ids, out_dtype=None) -> np.ndarray:
     return out.astype(out_dtype or ids.dtype).reshape(ids.shape)
 
 
+def local_ids(ids, expert_map) -> np.ndarray:
+    """Global routing ids -> this rank's local experts through vLLM's expert map
+    (vllm/model_executor/layers/fused_moe/expert_map_manager.py:22-113: ``map[g]`` is
+    the local index, -1 for another rank's expert).  Ids outside the map are -1."""
+    ids = np.asarray(ids).reshape(-1).astype(np.int64)
+    emap = np.asarray(expert_map).astype(np.int64)
+    ok = (ids >= 0) & (ids < emap.shape[0])
+    out = np.full(ids.shape, -1, dtype=np.int64)
+    out[ok] = emap[ids[ok]]
+    return out
+
+
+def compose_map(table: np.ndarray, expert_map) -> np.ndarray:
+    """Global id -> slot: ``table[map[g]]`` where ``map[g]`` names a local expert, else -1."""
+    emap = np.asarray(expert_map).astype(np.int64)
+    E = table.shape[0]
+    ok = (emap >= 0) & (emap < E)
+    out = np.full(emap.shape, -1, dtype=np.int32)
+    out[ok] = table[emap[ok]]
+    return out
+
+
+def manage_ep(st: CacheState, ids, expert_map, max_distinct: int, max_inserts: int,
+              policy: int, decay: int) -> tuple[list[tuple[int, int]], np.ndarray]:
+    """``expert_cache_manage_ep``: the reference manage step on the local ids, then the
+    composed global-id -> slot map.  The reference has no expert-parallel path (it
+    refuses such layers, vllm_expert_cache/backends/generic.py:145-149); this composes
+    its manage rules above with vLLM's expert map.  Map entries outside ``[0, E)`` are
+    treated like -1, as the kernel's bounds guard does."""
+    pairs = manage(st, local_ids(ids, expert_map), max_distinct, max_inserts, policy, decay)
+    return pairs, compose_map(st.table, expert_map)
+
+
 def gather(dsts, srcs, nbytes, miss, n_miss) -> None:
     """Byte copy of every installed miss: ``dst_k[slot] = src_k[expert]``.
 

@@ -69,7 +69,8 @@ class RoutedExperts(torch.nn.Module):
         for name, shape in extra:
             setattr(self, name, p(torch.randn(*shape)))
         self.global_num_experts = n_experts
-        self.expert_map = None
+        if not isinstance(getattr(type(self), "expert_map", None), property):
+            self.expert_map = None
 
 
 class QuantMethod:
@@ -445,3 +446,123 @@ def test_debug_trace_names_the_split(monkeypatch):
     x, w, ids = wide_step(5)
     m.apply(layer, x, w, ids)
     assert [x for x in log.msgs if "expert-cache debug" in x][0].endswith("-> split 3")
+
+
+# --- expert parallelism (EXPERT_CACHE_EP) ------------------------------------------------
+
+class EPExperts(RoutedExperts):
+    """vLLM's layout: the map is the ``_expert_map`` buffer behind a read-only property;
+    rank 0 of 2, round-robin (global 2j is local j); E local experts of 2E."""
+
+    def __init__(self, extra=()):
+        super().__init__(extra)
+        emap = torch.full((2 * E,), -1, dtype=torch.int32)
+        emap[0::2] = torch.arange(E, dtype=torch.int32)
+        self.register_buffer("_expert_map", emap)
+        self.global_num_experts = 2 * E
+        self.use_ep = True
+
+    @property
+    def expert_map(self):
+        return self._expert_map
+
+
+class Fmt:
+    def __init__(self, name):
+        self.name = name
+
+
+def ep_method(layer, fmt="Standard", supports=True, **kw):
+    m = QuantMethod(layer, **kw)
+    m.moe_kernel.prepare_finalize = type("PF", (), {"activation_format": Fmt(fmt)})()
+    m.moe_kernel.supports_expert_map = lambda: supports
+    m.apply_seen_map = None
+    stock = m.apply
+
+    def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
+              shared_experts_input=None):
+        m.apply_seen_map = layer.expert_map
+        return stock(layer, x, topk_weights, topk_ids, shared_experts, shared_experts_input)
+    m.apply = apply
+    return m
+
+
+def test_ep_refused_unless_opted_in():
+    layer = EPExperts()
+    ok, log = arm(layer, ep_method(layer))
+    assert not ok and log.said("expert parallelism active")
+
+
+def test_ep_layer_binds_the_composed_map(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = EPExperts(SCALES)
+    m = ep_method(layer, reads=["w13_weight_scale", "w2_weight_scale"])
+    ok, log = arm(layer, m)
+    assert ok, log.msgs
+    cache = layer._expert_cache
+    assert cache.E == E and cache.S == S
+    full = layer._expert_map
+    calls = []
+
+    def refresh_ep(ids, emap):
+        calls.append((ids.clone(), emap))
+        return torch.full((2 * E,), 5, dtype=torch.int32)
+    cache.refresh_ep = refresh_ep
+    cache.refresh = lambda ids: pytest.fail("an EP step must not remap the routing ids")
+    ids = torch.tensor([[0, 7, 2]], dtype=torch.int32)
+    m.apply(layer, torch.randn(1, H), torch.ones(1, 3), ids)
+    assert calls[0][1] is full                              # manage saw vLLM's own map
+    assert torch.equal(m.seen["ids"], ids)                  # ids stay global
+    assert (m.apply_seen_map == 5).all()                    # the kernel saw the composed map
+    assert m.seen["gne"] == 2 * E                           # global count unchanged
+    assert m.seen["w13"].data_ptr() == cache.slots["w13_weight"].data_ptr()
+    assert m.seen["cfg"]._w1.scale.size(0) == S
+    assert layer._expert_map is full and layer.global_num_experts == 2 * E
+    assert layer.w13_weight.size(0) == E
+
+
+def test_ep_wide_step_reads_through_with_vllms_map(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = EPExperts()
+    m = ep_method(layer)
+    assert arm(layer, m)[0]
+    layer._expert_cache.refresh_ep = lambda ids, emap: pytest.fail("wide step")
+    m.apply(layer, torch.randn(1, H), torch.ones(1, S + 1),
+            torch.zeros(1, S + 1, dtype=torch.int32))
+    assert m.apply_seen_map is layer._expert_map
+
+
+@pytest.mark.parametrize("setup,reason", [
+    (dict(fmt="BatchedExperts"), "BatchedExperts activation format"),
+    (dict(fmt=None), "unknown activation format"),
+    (dict(supports=False), "does not take an expert map"),
+    (dict(disable=True), "expert map disabled"),
+])
+def test_ep_refusals(monkeypatch, setup, reason):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = EPExperts()
+    m = ep_method(layer, fmt=setup.get("fmt", "Standard"), supports=setup.get("supports", True))
+    if setup.get("fmt", "x") is None:
+        m.moe_kernel.prepare_finalize = None
+    if setup.get("disable"):
+        m.disable_expert_map = True
+    ok, log = arm(layer, m)
+    assert not ok and log.said(reason), log.msgs
+
+
+def test_ep_without_a_map_is_refused(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = RoutedExperts()
+    layer.use_ep = True                    # EP on, but the kernel is given no map
+    ok, log = arm(layer, QuantMethod(layer))
+    assert not ok and log.said("without an expert_map")
+
+
+def test_ep_bookkeeping_buffers_are_not_mirrored(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = EPExperts()
+    layer.register_buffer("expert_local_to_global", torch.arange(E, dtype=torch.int64) * 2)
+    ok, log = arm(layer, ep_method(layer))
+    assert ok
+    assert "expert_local_to_global" not in layer._expert_cache.names
+    assert not log.said("not mirroring")

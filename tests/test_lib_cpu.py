@@ -26,7 +26,7 @@ def test_exports_every_header_symbol(h):
     import build_lib as b
     want = b.exported_symbols()
     assert set(want) == {"expert_cache_manage", "expert_cache_manage_remap",
-                         "expert_cache_gather"} | set(want)
+                         "expert_cache_manage_ep", "expert_cache_gather"} | set(want)
     out = subprocess.run(["nm", "-D", "--defined-only", str(b.OUT)], check=True,
                          capture_output=True, text=True).stdout
     have = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
@@ -63,6 +63,19 @@ def test_manage_remap_refuses_bad_output(h):
     bad = [NULL, 2, 0, 4, 8, 4, *([NULL] * 8), 0, 64]
     assert h.expert_cache_manage_remap(*bad, ctypes.cast(buf, ctypes.c_void_p), 4,
                                        NULL) == -1
+
+
+def test_manage_ep_refuses_bad_arguments(h):
+    buf = ctypes.cast(ctypes.create_string_buffer(64), ctypes.c_void_p)
+    state = [NULL] * 8
+
+    def ep(emap=buf, Eg=16, E=8, S=4, out=buf, policy=0):
+        return h.expert_cache_manage_ep(NULL, 2, emap, Eg, E, S, 8, 4, *state, policy, 64,
+                                        out, NULL)
+    assert ep(emap=NULL) == -1
+    assert ep(out=NULL) == -1
+    assert ep(Eg=0) == -1
+    assert ep(E=0) == -1 and ep(S=1025) == -1 and ep(policy=3) == -1
 
 
 def gather(h, sizes, chunks=16, lanes=64, ptr=256):

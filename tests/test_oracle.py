@@ -184,3 +184,21 @@ def test_align_oracle_hot_cold_split():
     np.testing.assert_array_equal(sc[:4], [1, 4, 7, 8])
     np.testing.assert_array_equal(ec[:2], [0, 4])
     assert (ec[2:] == -1).all()
+
+
+def test_manage_ep_known_answer():
+    """Rank 1 of 2, linear placement: global 4..7 are local 0..3.  Routing [5, 1, 6, -1,
+    9]: global 1 is another rank's expert, -1 padding, 9 outside the map; the local step
+    installs locals 1 and 2 into the two empty slots (ascending id, slots by (stamp,
+    slot)), and the composed map sends globals 5, 6 to slots 0, 1."""
+    emap = np.array([-1, -1, -1, -1, 0, 1, 2, 3], dtype=np.int32)
+    st = policy.CacheState(4, 2)
+    pairs, cmap = policy.manage_ep(st, [5, 1, 6, -1, 9], emap, 4, 2, policy.LRU, 0)
+    assert pairs == [(1, 0), (2, 1)]
+    assert st.table.tolist() == [-1, 0, 1, -1]
+    assert cmap.tolist() == [-1, -1, -1, -1, -1, 0, 1, -1]
+    assert st.routed.tolist() == [0, 1, 1, 0]
+    # next step: global 7 (local 3) evicts the older of the two unrouted slots
+    pairs, cmap = policy.manage_ep(st, [7, 6], emap, 4, 2, policy.LRU, 0)
+    assert pairs == [(3, 0)]
+    assert cmap.tolist() == [-1, -1, -1, -1, -1, -1, 1, 0]

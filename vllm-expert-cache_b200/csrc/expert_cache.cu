@@ -8,7 +8,10 @@
 //                  computed with warp ballots and three or four CTA barriers; results are
 //                  written straight back.  Optionally it ends with the routing remap
 //                  out_ids[i] = table[topk_ids[i]] on the updated table, so the separate
-//                  torch gather/cast kernels of the Python remap disappear.
+//                  torch gather/cast kernels of the Python remap disappear.  The
+//                  expert-parallel variant instead translates global ids through vLLM's
+//                  expert_map on load and ends by writing the composed global id -> slot
+//                  map.
 //
 //   gather_kernel  copies every missing expert's slabs from host memory (UVA views of
 //                  pinned pages) into its slot.  The work of all misses and all buffers is
@@ -73,7 +76,20 @@ struct ManageArgs {
   int policy, decay;
   void* out_ids;        // nullptr: no remap
   int out_elem_bytes;   // 4 or 8
+  // Expert parallelism (nullptr / 0 otherwise): routed ids are global and pass through
+  // emap [Eg] (global id -> local expert, -1 = another rank's); the launch ends by writing
+  // out_map [Eg] = the composed map global id -> slot (-1 = not resident here).
+  const int* emap;
+  int Eg;
+  int* out_map;
 };
+
+// A routed id as the policy sees it: the id itself or, under expert parallelism, the local
+// expert it maps to (-1 for another rank's expert and for ids outside the map).
+__device__ __forceinline__ int local_expert(const ManageArgs& a, int id) {
+  if (a.emap == nullptr) return id;
+  return (id >= 0 && id < a.Eg) ? a.emap[id] : -1;
+}
 
 // Dynamic shared memory: key[Spad] i64 | stamp[Spad] i64 | table[E] i32 | slot_expert[S]
 // i32 | routed flag[E] u8.  Spad = S rounded up to even so keys can be read in pairs.
@@ -155,7 +171,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   // ---- routed flags (duplicates write the same 1) ---------------------------------------
   if (my_id >= 0 && my_id < E) s_flag[my_id] = 1;
   for (int i = t + NT; i < a.mk; i += NT) {
-    const int e = a.ids[i];
+    const int e = local_expert(a, a.ids[i]);
     if (e >= 0 && e < E) s_flag[e] = 1;
   }
   __syncthreads();
@@ -273,8 +289,8 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   return true;
 }
 
-// expert_cache_manage / expert_cache_manage_remap: the policy step, then (optionally) the
-// remap of the routing ids on the updated table.
+// expert_cache_manage / _manage_remap / _manage_ep: the policy step, then (optionally)
+// the remap of the routing ids, or the composed expert-parallel map, on the updated table.
 template <int NT>
 __global__ void __launch_bounds__(NT, 1) manage_kernel(const __grid_constant__ ManageArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -282,11 +298,18 @@ __global__ void __launch_bounds__(NT, 1) manage_kernel(const __grid_constant__ M
   grid_dependency_wait();     // topk_ids may come from the kernel just before us
   release_dependents();       // let the gather launch and park on its own wait
   const int t = threadIdx.x;
-  const int my_id = (t < a.mk) ? a.ids[t] : -1;
+  const int my_id = (t < a.mk) ? local_expert(a, a.ids[t]) : -1;
   const bool changed = manage_core<NT>(a, sm, my_id);
-  if (a.out_ids) {
+  if (a.out_ids) {            // never set together with emap (host rule)
     if (changed) __syncthreads();
     remap_tail(a.ids, a.mk, a.E, a.out_ids, a.out_elem_bytes, sm.table, my_id, NT);
+  }
+  if (a.out_map) {
+    if (changed) __syncthreads();
+    for (int g = t; g < a.Eg; g += NT) {
+      const int e = a.emap[g];
+      a.out_map[g] = (e >= 0 && e < a.E) ? sm.table[e] : -1;
+    }
   }
 }
 
@@ -591,6 +614,9 @@ ManageArgs make_manage_args(const int* topk_ids, int mk, int E, int S, int max_d
   a.decay = decay;
   a.out_ids = nullptr;
   a.out_elem_bytes = 4;
+  a.emap = nullptr;
+  a.Eg = 0;
+  a.out_map = nullptr;
   return a;
 }
 
@@ -686,6 +712,21 @@ int expert_cache_manage_remap_noalloc(const int* topk_ids, int mk, int E, int S,
                                    map_cold, slot_expert, slot_stamp,
                                    static_cast<unsigned char*>(routed), step, miss, n_miss,
                                    policy, decay, out_ids, out_elem_bytes, stream);
+}
+
+int expert_cache_manage_ep(const int* topk_ids, int mk, const int* expert_map, int E_global,
+                           int E, int S, int max_distinct, int max_inserts, int* table,
+                           int* map_cold, int* slot_expert, long long* slot_stamp,
+                           unsigned char* routed, long long* step, int* miss, int* n_miss,
+                           int policy, int decay, int* out_map, cudaStream_t stream) {
+  if (expert_map == nullptr || out_map == nullptr || E_global <= 0) return -1;
+  ManageArgs a = make_manage_args(topk_ids, mk, E, S, max_distinct, max_inserts, table,
+                                  map_cold, slot_expert, slot_stamp, routed, step, miss,
+                                  n_miss, policy, decay);
+  a.emap = expert_map;
+  a.Eg = E_global;
+  a.out_map = out_map;
+  return manage_checked(a, stream);
 }
 
 int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void* s1,

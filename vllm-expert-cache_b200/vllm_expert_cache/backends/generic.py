@@ -15,7 +15,10 @@ stayed on full [E] storage, and wraps ``method.apply`` on the instance.  A cache
 swaps the slot buffers, the slot-bound config and ``global_num_experts = S`` in around the
 original ``apply`` and restores everything afterwards; a step wider than the slots calls
 the original untouched (or, opted in with EXPERT_CACHE_SPLIT_WIDE, runs as a few cached
-steps over consecutive token chunks).  The hook is vLLM's single post-load call site,
+steps over consecutive token chunks).  An expert-parallel layer (opted in with
+EXPERT_CACHE_EP) caches its local experts and keeps its routing ids global: the step
+binds a composed global id -> slot map as ``layer.expert_map`` instead of remapping the
+ids.  The hook is vLLM's single post-load call site,
 ``model_loader.utils.process_weights_after_loading``, rebound wherever it was imported by
 name.  Refusals are logged and leave the layer on the stock path.
 """
@@ -36,6 +39,10 @@ _QUANT_DESCS = ("_a1", "_a2", "_w1", "_w2")
 _QUANT_FIELDS = ("scale", "alpha_or_gscale", "zp", "bias")
 # Registered names of the two expert weight matrices, plain and packed spellings.
 _WEIGHT_PAIRS = (("w13_weight", "w2_weight"), ("w13_weight_packed", "w2_weight_packed"))
+# Expert-parallel bookkeeping vLLM registers on the layer (fused_moe/layer.py:516-531):
+# indexed by expert id but not expert data, so never mirrored into slots.
+_EP_BUFFERS = frozenset({"_expert_map", "expert_mask", "expert_global_to_physical",
+                         "expert_physical_to_global", "expert_local_to_global"})
 # Activation quant dtypes whose scales are per block of one row (vLLM's string dtypes).
 _MICRO_SCALED = frozenset({"nvfp4", "mxfp4", "mxfp6_e3m2", "mxfp6_e2m3", "mxfp8"})
 
@@ -68,6 +75,8 @@ def _per_expert_tensors(layer, num_experts: int) -> dict[str, list[str]]:
         ((k, v) for k, v in vars(layer).items() if isinstance(v, torch.Tensor)))
     for name, t in found:
         if not isinstance(t, torch.Tensor) or t.dim() < 1 or t.size(0) != num_experts:
+            continue
+        if name in _EP_BUFFERS:
             continue
         names = by_storage.setdefault(t.data_ptr(), [])
         if name not in names:
@@ -145,8 +154,42 @@ def _decline(layer, method, num_experts: int) -> str | None:
     if getattr(kernel, "fused_experts", None) is None:
         return "moe_kernel exposes no fused_experts to rebind"
     if getattr(layer, "expert_map", None) is not None:
-        return "expert parallelism active (layer.expert_map is set)"
+        if not settings.ep:
+            return "expert parallelism active (layer.expert_map is set)"
+        return _decline_ep(method, kernel)
+    if getattr(layer, "use_ep", False):
+        # EP whose kernel takes no expert map: routing ids are global while the layer's
+        # weights are local, so a slot remap over the local count would be meaningless.
+        return "expert parallelism without an expert_map (the kernel is not given one)"
     return None
+
+
+def _decline_ep(method, kernel) -> str | None:
+    """Why an expert-parallel layer cannot be cached through its expert map, or None.
+
+    The composed map only works where the stock kernel reaches every expert through
+    ``layer.expert_map``: the method passes it (``disable_expert_map`` unset,
+    vllm/model_executor/layers/fused_moe/fused_moe_modular_method.py:36-40, 108), the
+    kernel supports it, and tokens arrive in the standard (num_tokens, hidden) format;
+    batched all-to-all formats index experts by local position instead.
+    """
+    if getattr(method, "disable_expert_map", False):
+        return "expert parallelism with the expert map disabled for this method"
+    supports = getattr(kernel, "supports_expert_map", None)
+    if callable(supports) and not supports():
+        return "expert parallelism with a kernel that does not take an expert map"
+    fmt = getattr(getattr(kernel, "prepare_finalize", None), "activation_format", None)
+    name = getattr(fmt, "name", None)
+    if name != "Standard":
+        return (f"expert parallelism with the {name or 'unknown'} activation format (only "
+                "the standard format reaches the experts through expert_map)")
+    return None
+
+
+def _expert_map_name(layer) -> str:
+    """Where ``layer.expert_map`` is stored: vLLM registers it as the ``_expert_map``
+    buffer behind a read-only property (fused_moe/layer.py:516-521, 1318-1322)."""
+    return "_expert_map" if "_expert_map" in layer._buffers else "expert_map"
 
 
 def _weight_names(layer) -> tuple[str, str] | None:
@@ -219,6 +262,8 @@ def arm(layer, method, logger) -> bool:
 
     stock_apply = method.apply
     debug_left = [settings.debug_calls]
+    ep_name = _expert_map_name(layer) if getattr(layer, "expert_map", None) is not None \
+        else None
     split_max = settings.split_wide
     if split_max:
         why = _token_local(slot_cfg)
@@ -228,18 +273,27 @@ def arm(layer, method, logger) -> bool:
     split = [split_max]
 
     def cached(layer, x, topk_weights, topk_ids, shared_experts, shared_experts_input):
-        slot_ids = cache.refresh(topk_ids)
         experts = method.moe_kernel.fused_experts
         saved = (experts.quant_config, method.moe_quant_config, layer.global_num_experts)
+        if ep_name is None:
+            ids = cache.refresh(topk_ids)
+            layer.global_num_experts = cache.S
+        else:
+            # Expert parallel: the routing ids stay global; the layer's expert map is
+            # replaced by the composed global id -> slot map for this step.
+            ids = topk_ids
+            full_map = getattr(layer, ep_name)
+            _set_tensor(layer, ep_name, cache.refresh_ep(topk_ids, full_map))
         experts.quant_config = slot_cfg
         method.moe_quant_config = slot_cfg
-        layer.global_num_experts = cache.S
         try:
             with _slot_bound(layer, cache):
-                return stock_apply(layer, x, topk_weights, slot_ids, shared_experts,
+                return stock_apply(layer, x, topk_weights, ids, shared_experts,
                                    shared_experts_input)
         finally:
             experts.quant_config, method.moe_quant_config, layer.global_num_experts = saved
+            if ep_name is not None:
+                _set_tensor(layer, ep_name, full_map)
 
     def chunk_tokens(x, topk_ids, shared_experts) -> int:
         """Tokens per chunk when this wide step may be split, else 0 (read through)."""

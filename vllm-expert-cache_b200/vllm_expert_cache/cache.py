@@ -133,6 +133,36 @@ class ExpertSlotCache:
         self._gather(h, stream)
         return out if wide else out.to(topk_ids.dtype)
 
+    def refresh_ep(self, topk_ids: torch.Tensor, expert_map: torch.Tensor) -> torch.Tensor:
+        """One cached step of an expert-parallel layer.
+
+        ``topk_ids`` are global expert ids and ``expert_map`` (int32 [E_global], vLLM's
+        global id -> local expert or -1) selects this rank's experts, which are the
+        cache's E.  Returns the composed map global id -> slot (int32 [E_global], -1 where
+        the expert is not resident here) to pass as the stock kernel's ``expert_map``; the
+        routing ids themselves stay global.  One ``expert_cache_manage_ep`` launch, then
+        the gather.
+        """
+        h = lib()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        ids = topk_ids
+        if ids.dtype != torch.int32 or not ids.is_contiguous():
+            ids = ids.to(torch.int32).contiguous()
+        emap = expert_map
+        if emap.dtype != torch.int32 or not emap.is_contiguous():
+            emap = emap.to(torch.int32).contiguous()
+        mk = ids.numel()
+        out = torch.empty((emap.numel(),), dtype=torch.int32, device=self.device)
+        rc = h.expert_cache_manage_ep(
+            _ptr(ids), mk, _ptr(emap), emap.numel(), self.E, self.S, min(self.E, mk),
+            self.S, *self._state(), self.policy, self.decay, _ptr(out), stream)
+        if rc != 0:
+            raise RuntimeError(f"expert_cache_manage_ep failed rc={rc}")
+        if self.miss_total is not None:
+            self.miss_total.add_(self.n_miss)
+        self._gather(h, stream)
+        return out
+
     def stats(self) -> dict:
         """Host snapshot of the counters (synchronises; call outside the hot path)."""
         out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item())}

@@ -21,6 +21,9 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
                                   cached chunks of S // top_k tokens when the layer's
                                   activation quantisation is per token (new, off by
                                   default: 0 keeps the reference's read-through)
+  EXPERT_CACHE_EP         0       '1' caches expert-parallel layers (standard activation
+                                  format, vLLM expert_map) instead of refusing them as the
+                                  reference does (new, off by default)
 
 ``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
 """
@@ -81,6 +84,10 @@ class Settings:
     @property
     def split_wide(self) -> int:
         return max(0, int(_env("EXPERT_CACHE_SPLIT_WIDE", "0") or 0))
+
+    @property
+    def ep(self) -> bool:
+        return _env("EXPERT_CACHE_EP", "0") == "1"
 
     def slots_for(self, num_experts: int) -> int:
         want = self.slots
