@@ -103,6 +103,60 @@ EXPERT_CACHE_API int expert_cache_manage_ep(
     long long* slot_stamp, unsigned char* routed, long long* step, int* miss, int* n_miss,
     int policy, int decay, int* out_map, cudaStream_t stream);
 
+/* Install predicted experts ahead of their layer's step (next-layer prefetch).
+ *
+ * Arguments are expert_cache_manage's without `decay`. pred_ids are the predicted
+ * routing. The call installs the missing ones exactly as a manage step would:
+ *   - same victim order;
+ *   - new slots get priority `step` (LRU) or 1 (LFU);
+ *   - miss list and n_miss are written for a following expert_cache_gather.
+ *
+ * Nothing else changes:
+ *   - `step` does not advance;
+ *   - hits keep their priority;
+ *   - no ageing runs.
+ *
+ * A wrong prediction therefore costs transfers and evictions, never results: the
+ * layer's own step still installs whatever it routes.
+ *
+ * Returns -1 on the manage rules.
+ *
+ * Has no counterpart in the reference: its README names next-layer prefetch as
+ * unexplored (README.md:392-394). */
+EXPERT_CACHE_API int expert_cache_prefetch(
+    const int* pred_ids, int mk, int E, int S, int max_distinct, int max_inserts, int* table,
+    int* map_cold, int* slot_expert, long long* slot_stamp, unsigned char* routed,
+    long long* step, int* miss, int* n_miss, int policy, cudaStream_t stream);
+
+/* Limits of expert_cache_pregate. Its shared memory holds one token row and E scores. */
+#define EXPERT_CACHE_PREGATE_MAX_HIDDEN 16384
+#define EXPERT_CACHE_PREGATE_MAX_EXPERTS 2048
+
+/* Predict a layer's routing from a hidden state.
+ *
+ * For each of T tokens, out_ids[t*k + r] is the r-th highest score over the E experts,
+ * where the score is the dot product of x[t, :H] (bf16, row stride ldx elements) with
+ * gate_w[e, :H] (bf16, [E, H] row-major: a router's weight), accumulated in fp32.
+ *   - Ties go to the lower expert id.
+ *   - NaN scores are never picked.
+ *   - Fewer than k finite scores leave -1.
+ * Softmax and renormalisation are monotonic, so this is the router's own top-k for the
+ * given input. Grouped or biased routers are only approximated. One CTA per token.
+ *
+ * Returns -1 if:
+ *   - T < 0;
+ *   - H <= 0, H % 8 != 0 or H > EXPERT_CACHE_PREGATE_MAX_HIDDEN;
+ *   - ldx < H or ldx % 8 != 0;
+ *   - E <= 0 or E > EXPERT_CACHE_PREGATE_MAX_EXPERTS;
+ *   - k outside [1, 32];
+ *   - x or gate_w is not 16-byte aligned.
+ * T == 0 enqueues nothing.
+ *
+ * Has no counterpart in the reference. */
+EXPERT_CACHE_API int expert_cache_pregate(const void* x, int T, int ldx, int H,
+                                          const void* gate_w, int E, int k, int* out_ids,
+                                          cudaStream_t stream);
+
 /* Largest expert count of expert_cache_fused (reference expert_cache.hip:341, MAXE). */
 #define EXPERT_CACHE_FUSED_MAX_EXPERTS 1024
 

@@ -202,6 +202,70 @@ def manage_ep(st: CacheState, ids, expert_map, max_distinct: int, max_inserts: i
     return pairs, compose_map(st.table, expert_map)
 
 
+def prefetch(st: CacheState, ids, max_distinct: int, max_inserts: int,
+             policy: int) -> list[tuple[int, int]]:
+    """``expert_cache_prefetch``: install the predicted experts that are missing, with the
+    victim order and install rules of :func:`manage`, and change nothing else -- ``step``
+    does not advance, hits keep their priority, no ageing.  New slots take priority
+    ``step`` (LRU) or 1 (LFU).  The reference has no prefetch (its README.md:392-394
+    names it as unexplored); the rules are the manage rules above minus the step's own
+    bookkeeping."""
+    E, S = st.E, st.S
+    ids = np.asarray(ids).reshape(-1).astype(np.int64)
+    now = int(st.step[0])
+    st.n_miss[0] = 0
+    st.routed[:] = 0
+    st.routed[ids[(ids >= 0) & (ids < E)]] = 1
+    routed = np.flatnonzero(st.routed)
+    if routed.size > max_distinct:
+        return []
+    missing = [e for e in routed.tolist() if st.table[e] < 0]
+    nins = min(len(missing), max_inserts)
+    if nins <= 0:
+        return []
+    for j in range(nins):
+        st.miss[2 * j] = missing[j]
+    se, stamp = st.slot_expert, st.slot_stamp
+    evictable = [i for i in range(S)
+                 if se[i] < 0 or se[i] >= E or not st.routed[se[i]]]
+    evictable.sort(key=lambda i: (int(stamp[i]), i))
+    fresh = now if policy == LRU else 1
+    out = []
+    for r, sl in enumerate(evictable[:nins]):
+        e = missing[r]
+        old = int(se[sl])
+        if old >= 0:
+            st.table[old] = -1
+            st.map_cold[old] = old
+        se[sl] = e
+        stamp[sl] = fresh
+        st.table[e] = sl
+        st.map_cold[e] = -1
+        st.miss[2 * r + 1] = sl
+        out.append((e, sl))
+    st.n_miss[0] = len(out)
+    return out
+
+
+def pregate_scores(x, gate_w) -> np.ndarray:
+    """``x[t] . gate_w[e]`` in float64 from the bf16 values (given as float arrays)."""
+    return np.asarray(x, dtype=np.float64) @ np.asarray(gate_w, dtype=np.float64).T
+
+
+def pregate(x, gate_w, k: int) -> np.ndarray:
+    """``expert_cache_pregate``: per token, the k highest scores' expert ids, ties to the
+    lower id, NaN never chosen, -1 where fewer than k scores are finite."""
+    sc = pregate_scores(x, gate_w)
+    T, E = sc.shape
+    out = np.full((T, k), -1, dtype=np.int32)
+    for t in range(T):
+        order = sorted((e for e in range(E) if not np.isnan(sc[t, e])),
+                       key=lambda e: (-sc[t, e], e))
+        take = order[:k]
+        out[t, :len(take)] = take
+    return out
+
+
 def gather(dsts, srcs, nbytes, miss, n_miss) -> None:
     """Byte copy of every installed miss: ``dst_k[slot] = src_k[expert]``.
 

@@ -566,3 +566,67 @@ def test_ep_bookkeeping_buffers_are_not_mirrored(monkeypatch):
     assert ok
     assert "expert_local_to_global" not in layer._expert_cache.names
     assert not log.said("not mirroring")
+
+
+# --- next-layer prefetch linking (EXPERT_CACHE_PREFETCH) ---------------------------------
+
+def gated(gate=None):
+    layer = RoutedExperts()
+    w = torch.randn(E, 64).to(torch.bfloat16) if gate is None else gate
+    layer.runner = type("Runner", (), {})()
+    layer.runner.gate = torch.nn.Linear(64, E, bias=False)
+    layer.runner.gate.weight = torch.nn.Parameter(w, requires_grad=False)
+    return layer
+
+
+def armed_chain(layers):
+    chain = []
+    for ly in layers:
+        assert arm(ly, QuantMethod(ly))[0]
+        chain.append((ly, ly._expert_cache))
+    return chain
+
+
+def test_prefetch_links_consecutive_layers_with_usable_routers():
+    bad_dtype = gated(torch.randn(E, 64))                        # fp32 router
+    bad_width = gated(torch.randn(E, 60).to(torch.bfloat16))     # hidden % 8 != 0
+    layers = [gated(), gated(), bad_dtype, gated(), bad_width]
+    chain = armed_chain(layers)
+    log = Log()
+    assert generic._link_prefetch(chain, log) == 2
+    caches = [c for _, c in chain]
+    assert caches[0].next is caches[1]
+    assert caches[0].next_gate is layers[1].runner.gate.weight
+    assert caches[0].pred.shape == (S,) and caches[0].pred.dtype == torch.int32
+    assert caches[1].next is None                 # the next router is fp32
+    assert caches[2].next is caches[3]
+    assert caches[3].next is None and caches[4].next is None
+    assert log.said("not bf16") and log.said("layout")
+
+
+def test_prefetch_skips_layers_without_a_router():
+    plain = RoutedExperts()
+    chain = armed_chain([gated(), plain])
+    log = Log()
+    assert generic._link_prefetch(chain, log) == 0
+    assert log.said("no router weight")
+
+
+def test_prefetch_not_linked_across_expert_parallel_layers(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    ep = EPExperts()
+    ep.runner = gated().runner
+    assert arm(ep, ep_method(ep))[0]
+    first = gated()
+    assert arm(first, QuantMethod(first))[0]
+    chain = [(first, first._expert_cache), (ep, ep._expert_cache)]
+    assert generic._link_prefetch(chain, Log()) == 0
+
+
+def test_prefetch_is_skipped_while_vllm_captures_piecewise(monkeypatch):
+    import vllm.forward_context as fc
+    monkeypatch.setattr(fc, "is_forward_context_available", lambda: True)
+    for name, allowed in (("PIECEWISE", False), ("FULL", True), ("NONE", True)):
+        ctx = type("Ctx", (), {"cudagraph_runtime_mode": type("M", (), {"name": name})()})()
+        monkeypatch.setattr(fc, "get_forward_context", lambda c=ctx: c)
+        assert generic._prefetch_allowed() == allowed, name

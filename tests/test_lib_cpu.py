@@ -26,7 +26,8 @@ def test_exports_every_header_symbol(h):
     import build_lib as b
     want = b.exported_symbols()
     assert set(want) == {"expert_cache_manage", "expert_cache_manage_remap",
-                         "expert_cache_manage_ep", "expert_cache_gather"} | set(want)
+                         "expert_cache_manage_ep", "expert_cache_prefetch",
+                         "expert_cache_pregate", "expert_cache_gather"} | set(want)
     out = subprocess.run(["nm", "-D", "--defined-only", str(b.OUT)], check=True,
                          capture_output=True, text=True).stdout
     have = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
@@ -76,6 +77,28 @@ def test_manage_ep_refuses_bad_arguments(h):
     assert ep(out=NULL) == -1
     assert ep(Eg=0) == -1
     assert ep(E=0) == -1 and ep(S=1025) == -1 and ep(policy=3) == -1
+
+
+def test_prefetch_refuses_bad_arguments(h):
+    def pf(E=8, S=4, mi=4, policy=0):
+        return h.expert_cache_prefetch(NULL, 2, E, S, 8, mi, *([NULL] * 8), policy, NULL)
+    assert pf(E=0) == -1 and pf(S=0) == -1 and pf(mi=-1) == -1 and pf(policy=2) == -1
+
+
+@pytest.mark.parametrize("kw", [dict(T=-1), dict(H=0), dict(H=12), dict(H=16392),
+                                dict(ldx=8), dict(ldx=20), dict(E=0), dict(E=2049),
+                                dict(k=0), dict(k=33), dict(x=8), dict(w=24)])
+def test_pregate_refuses_bad_arguments(h, kw):
+    a = dict(T=2, ldx=16, H=16, E=8, k=4, x=256, w=512)
+    a.update(kw)
+    out = ctypes.c_void_p(1024)
+    assert h.expert_cache_pregate(ctypes.c_void_p(a["x"]), a["T"], a["ldx"], a["H"],
+                                  ctypes.c_void_p(a["w"]), a["E"], a["k"], out, NULL) == -1
+
+
+def test_pregate_empty_batch_enqueues_nothing(h):
+    assert h.expert_cache_pregate(ctypes.c_void_p(256), 0, 16, 16, ctypes.c_void_p(512), 8,
+                                  4, ctypes.c_void_p(1024), NULL) == 0
 
 
 def gather(h, sizes, chunks=16, lanes=64, ptr=256):

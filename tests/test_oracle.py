@@ -202,3 +202,43 @@ def test_manage_ep_known_answer():
     pairs, cmap = policy.manage_ep(st, [7, 6], emap, 4, 2, policy.LRU, 0)
     assert pairs == [(3, 0)]
     assert cmap.tolist() == [-1, -1, -1, -1, -1, -1, 1, 0]
+
+
+def test_prefetch_known_answer():
+    """Prefetch installs missing predicted experts without the step's bookkeeping: step
+    stays, the resident predicted expert keeps its priority, new slots take priority
+    ``step`` (LRU)."""
+    st = policy.CacheState(8, 3)
+    policy.manage(st, [1, 2], 8, 3, policy.LRU, 0)            # step 1: 1->s0, 2->s1
+    policy.manage(st, [2], 8, 3, policy.LRU, 0)               # step 2: 2 refreshed
+    assert st.slot_stamp.tolist() == [1, 2, 0]
+    pairs = policy.prefetch(st, [2, 5, 6], 8, 3, policy.LRU)
+    # victims: empty slot 2 (stamp 0), then slot 0 (expert 1, stamp 1); slot 1 is parked
+    assert pairs == [(5, 2), (6, 0)]
+    assert int(st.step[0]) == 2
+    assert st.slot_stamp.tolist() == [2, 2, 2]
+    assert st.table[1] == -1 and st.map_cold[1] == 1 and st.table[2] == 1
+    assert int(st.n_miss[0]) == 2
+    # a real step afterwards sees the prefetched experts as hits
+    assert policy.manage(st, [5, 6], 8, 3, policy.LRU, 0) == []
+
+
+def test_prefetch_lfu_keeps_counts_and_skips_ageing():
+    st = policy.CacheState(6, 2)
+    for _ in range(4):
+        policy.manage(st, [0], 6, 2, policy.LFU, 2)
+    before = st.slot_stamp.copy()
+    policy.prefetch(st, [0, 3], 6, 2, policy.LFU)
+    s0 = int(st.table[0])
+    assert st.slot_stamp[s0] == before[s0]                    # no refresh, no halving
+    assert st.slot_stamp[int(st.table[3])] == 1
+
+
+def test_pregate_oracle_ties_and_nan():
+    x = np.array([[1.0, 0.0], [0.0, 0.0]])
+    w = np.array([[1.0, 0.0], [1.0, 0.0], [np.nan, 0.0], [2.0, 0.0]])
+    got = policy.pregate(x, w, 3)
+    assert got[0].tolist() == [3, 0, 1]                       # tie 0/1 -> lower id first
+    assert got[1].tolist() == [0, 1, 3]                       # all zero: ascending ids
+    got = policy.pregate(x, w, 4)
+    assert got[0].tolist() == [3, 0, 1, -1]                   # NaN never chosen

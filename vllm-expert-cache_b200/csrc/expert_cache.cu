@@ -31,6 +31,7 @@
 // :106-189 (victim choice), :286-314 (gather) and the remap of
 // vllm_expert_cache/cache.py:108-110; the C-ABI at the bottom keeps the reference's
 // symbols, argument order and return codes (expert_cache.hip:590-645).
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -82,6 +83,9 @@ struct ManageArgs {
   const int* emap;
   int Eg;
   int* out_map;
+  // Prefetch (expert_cache_prefetch): install the predicted experts that are missing and
+  // change nothing else -- no step advance, no priority refresh of hits, no ageing.
+  int prefetch;
 };
 
 // A routed id as the policy sees it: the id itself or, under expert parallelism, the local
@@ -156,7 +160,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
 
   // ---- one round of loads: step, table, slot state (ids were read by the caller) -------
-  const long long now = a.step[0] + 1;
+  const long long now = a.step[0] + (a.prefetch ? 0 : 1);
   for (int e = t; e < E; e += NT) {
     s_tab[e] = a.table[e];
     s_flag[e] = 0;
@@ -166,7 +170,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
     s_st[s] = a.slot_stamp[s];
   }
   __syncthreads();
-  if (t == 0) a.step[0] = now;   // every thread has read the old value above
+  if (t == 0 && !a.prefetch) a.step[0] = now;   // every thread read the old value above
 
   // ---- routed flags (duplicates write the same 1) ---------------------------------------
   if (my_id >= 0 && my_id < E) s_flag[my_id] = 1;
@@ -185,7 +189,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
     parked = se >= 0 && se < E && s_flag[se];
     hit = parked && s_tab[se] == t;
     stamp = s_st[t];
-    if (hit) stamp = (a.policy == 0) ? now : stamp + 1;
+    if (hit && !a.prefetch) stamp = (a.policy == 0) ? now : stamp + 1;
   }
   {
     const unsigned b = __ballot_sync(0xffffffffu, t < S && !parked);
@@ -238,7 +242,8 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   }
 
   // ---- ageing, eviction keys, miss list -------------------------------------------------
-  const bool age = a.policy != 0 && a.decay > 0 && (now % (long long)a.decay) == 0;
+  const bool age = !a.prefetch && a.policy != 0 && a.decay > 0 &&
+                   (now % (long long)a.decay) == 0;
   if (t < S) {
     if (age) stamp >>= 1;
     s_st[t] = stamp;
@@ -519,6 +524,84 @@ __global__ void __launch_bounds__(kGatherThreads)
 }
 
 // ---------------------------------------------------------------------------------------
+// pregate: the next layer's routing predicted from this layer's MoE input
+
+constexpr int kPregateThreads = 256;
+
+// One CTA per token.  The token's row is staged in shared memory; each warp scores whole
+// experts (16-byte loads of the gate row, fp32 accumulation, a fixed xor-shuffle order),
+// then k rounds of a CTA argmax pick the top k (ties -> lower expert id; NaN never wins;
+// fewer than k finite scores leave -1).
+__global__ void __launch_bounds__(kPregateThreads)
+    pregate_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int H,
+                   const __nv_bfloat16* __restrict__ w, int E, int k, int* __restrict__ out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint4* xs = reinterpret_cast<uint4*>(smem);                                  // [H/8]
+  float* logit = reinterpret_cast<float*>(smem + (size_t)H * 2);                // [E]
+  __shared__ float r_val[kPregateThreads / 32];
+  __shared__ int r_idx[kPregateThreads / 32];
+  constexpr int NW = kPregateThreads / 32;
+  const int tok = blockIdx.x, t = threadIdx.x, lane = t & 31, wp = t >> 5;
+  const int hv = H >> 3;
+
+  grid_dependency_wait();
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)tok * ldx);
+  for (int i = t; i < hv; i += kPregateThreads) xs[i] = xr[i];
+  __syncthreads();
+
+  for (int e = wp; e < E; e += NW) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)e * H);
+    float acc = 0.f;
+    for (int i = lane; i < hv; i += 32) {
+      const uint4 a = xs[i];
+      const uint4 b = wr[i];
+      const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* pb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fa = __bfloat1622float2(pa[j]);
+        const float2 fb = __bfloat1622float2(pb[j]);
+        acc = fmaf(fa.x, fb.x, acc);
+        acc = fmaf(fa.y, fb.y, acc);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) logit[e] = acc;
+  }
+  __syncthreads();
+
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int e = t; e < E; e += kPregateThreads) {
+      const float v = logit[e];
+      if (v > bv) { bv = v; bi = e; }        // ascending e: the first of equals stays
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { r_val[wp] = bv; r_idx[wp] = bi; }
+    __syncthreads();
+    if (t == 0) {
+      float v = -INFINITY;
+      int b = -1;
+      for (int q = 0; q < NW; ++q)
+        if (r_idx[q] >= 0 && (b < 0 || r_val[q] > v || (r_val[q] == v && r_idx[q] < b))) {
+          v = r_val[q];
+          b = r_idx[q];
+        }
+      out[(size_t)tok * k + r] = b;
+      if (b >= 0) logit[b] = -INFINITY;       // taken: never picked again
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // host side
 
 int current_device() {
@@ -617,6 +700,7 @@ ManageArgs make_manage_args(const int* topk_ids, int mk, int E, int S, int max_d
   a.emap = nullptr;
   a.Eg = 0;
   a.out_map = nullptr;
+  a.prefetch = 0;
   return a;
 }
 
@@ -727,6 +811,40 @@ int expert_cache_manage_ep(const int* topk_ids, int mk, const int* expert_map, i
   a.Eg = E_global;
   a.out_map = out_map;
   return manage_checked(a, stream);
+}
+
+int expert_cache_prefetch(const int* pred_ids, int mk, int E, int S, int max_distinct,
+                          int max_inserts, int* table, int* map_cold, int* slot_expert,
+                          long long* slot_stamp, unsigned char* routed, long long* step,
+                          int* miss, int* n_miss, int policy, cudaStream_t stream) {
+  ManageArgs a = make_manage_args(pred_ids, mk, E, S, max_distinct, max_inserts, table,
+                                  map_cold, slot_expert, slot_stamp, routed, step, miss,
+                                  n_miss, policy, 0);
+  a.prefetch = 1;
+  return manage_checked(a, stream);
+}
+
+int expert_cache_pregate(const void* x, int T, int ldx, int H, const void* gate_w, int E,
+                         int k, int* out_ids, cudaStream_t stream) {
+  if (T < 0 || H <= 0 || H % 8 || H > EXPERT_CACHE_PREGATE_MAX_HIDDEN || ldx < H || ldx % 8)
+    return -1;
+  if (E <= 0 || E > EXPERT_CACHE_PREGATE_MAX_EXPERTS || k <= 0 || k > 32) return -1;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(gate_w)) & 15) return -1;
+  if (T == 0) return 0;
+  if (x == nullptr || gate_w == nullptr || out_ids == nullptr) return -1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)T);
+  cfg.blockDim = dim3(kPregateThreads);
+  cfg.dynamicSmemBytes = (size_t)H * 2 + (size_t)E * 4;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, pregate_kernel,
+                                 static_cast<const __nv_bfloat16*>(x), ldx, H,
+                                 static_cast<const __nv_bfloat16*>(gate_w), E, k, out_ids);
 }
 
 int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void* s1,

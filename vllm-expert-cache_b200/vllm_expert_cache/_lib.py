@@ -3,8 +3,8 @@
 Search order, as in the reference (vllm_expert_cache/_lib.py:17-33): $EXPERT_CACHE_LIB,
 then ``libexpertcache.so`` beside this package, then /usr/local/lib.  A missing library
 raises FileNotFoundError; there is no fallback path.  The handle is loaded once per
-process.  Argument types are the reference's (_lib.py:41-53) plus the fused-remap and
-expert-parallel entry points this build adds.
+process.  Argument types are the reference's (_lib.py:41-53) plus the fused-remap,
+expert-parallel and prefetch entry points this build adds.
 """
 
 from __future__ import annotations
@@ -20,6 +20,8 @@ _P, _I, _L = ctypes.c_void_p, ctypes.c_int, ctypes.c_long
 MANAGE_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P]
 MANAGE_REMAP_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P, _I, _P]
 MANAGE_EP_ARGTYPES = [_P, _I, _P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P, _P]
+PREFETCH_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I, _P]
+PREGATE_ARGTYPES = [_P, _I, _I, _I, _P, _I, _I, _P, _P]
 GATHER_ARGTYPES = [_P, _P, _L] * GATHER_SLOTS + [_P, _P, _I, _I, _P]
 
 _handle = None
@@ -48,6 +50,10 @@ def bind(h: ctypes.CDLL) -> ctypes.CDLL:
     h.expert_cache_manage_remap.argtypes = MANAGE_REMAP_ARGTYPES
     h.expert_cache_manage_ep.restype = _I
     h.expert_cache_manage_ep.argtypes = MANAGE_EP_ARGTYPES
+    h.expert_cache_prefetch.restype = _I
+    h.expert_cache_prefetch.argtypes = PREFETCH_ARGTYPES
+    h.expert_cache_pregate.restype = _I
+    h.expert_cache_pregate.argtypes = PREGATE_ARGTYPES
     h.expert_cache_gather.restype = _I
     h.expert_cache_gather.argtypes = GATHER_ARGTYPES
     return h

@@ -47,6 +47,8 @@ _EP_BUFFERS = frozenset({"_expert_map", "expert_mask", "expert_global_to_physica
 _MICRO_SCALED = frozenset({"nvfp4", "mxfp4", "mxfp6_e3m2", "mxfp6_e2m3", "mxfp8"})
 
 _installed = False
+# One side stream per device carries every layer's next-layer prefetch.
+_side_streams: dict[int, torch.cuda.Stream] = {}
 
 
 def _set_tensor(layer, name: str, t: torch.Tensor) -> None:
@@ -192,6 +194,97 @@ def _expert_map_name(layer) -> str:
     return "_expert_map" if "_expert_map" in layer._buffers else "expert_map"
 
 
+def _router_weight(layer) -> torch.Tensor | None:
+    """The layer's router weight [E, hidden]: vLLM hands the model's gate to FusedMoE,
+    which keeps it on its runner (fused_moe/layer.py:426-431, runner/moe_runner.py:238)."""
+    for owner in (getattr(layer, "runner", None), layer):
+        w = getattr(getattr(owner, "gate", None), "weight", None)
+        if isinstance(w, torch.Tensor):
+            return w
+    return None
+
+
+def _prefetch_unusable(w: torch.Tensor | None, cache: ExpertSlotCache) -> str | None:
+    """Why the pregate kernel cannot score with this router weight, or None."""
+    if w is None:
+        return "no router weight on the layer"
+    if w.dtype != torch.bfloat16 or w.dim() != 2 or w.size(0) != cache.E:
+        return f"router weight {tuple(w.shape)} {w.dtype} is not bf16 [{cache.E}, hidden]"
+    if not w.is_contiguous() or w.size(1) % 8 or w.size(1) > 16384 or w.data_ptr() % 16:
+        return "router weight layout (contiguous rows, hidden % 8, <= 16384, 16 B aligned)"
+    if cache.E > 2048:
+        return "more than 2048 experts"
+    return None
+
+
+def _link_prefetch(armed: list, logger) -> int:
+    """Chain consecutive armed layers so each predicts and prefetches the next one's
+    experts.  ``armed``: (layer, cache) in model order.  Expert-parallel layers are not
+    linked (their routing ids are global, their caches local)."""
+    linked = 0
+    for (li, ci), (lj, cj) in zip(armed, armed[1:]):
+        if getattr(li, "expert_map", None) is not None or \
+                getattr(lj, "expert_map", None) is not None:
+            continue
+        w = _router_weight(lj)
+        why = _prefetch_unusable(w, cj)
+        if why is not None:
+            logger.info("expert-cache: no prefetch into %s -- %s", type(lj).__name__, why)
+            continue
+        ci.next, ci.next_gate = cj, w
+        ci.pred = torch.empty((ci.S,), dtype=torch.int32, device=ci.device)
+        linked += 1
+    return linked
+
+
+def _prefetch_allowed() -> bool:
+    """A fork must be joined inside the same CUDA graph: allowed eagerly and in vLLM's
+    FULL graphs, not while it captures PIECEWISE graphs (the next layer's MoE lies in
+    another piece)."""
+    try:
+        from vllm.forward_context import get_forward_context, is_forward_context_available
+    except Exception:
+        return True
+    if not is_forward_context_available():
+        return True
+    mode = getattr(get_forward_context(), "cudagraph_runtime_mode", None)
+    return getattr(mode, "name", "NONE") != "PIECEWISE"
+
+
+def _fork_prefetch(cache: ExpertSlotCache, x: torch.Tensor, k: int) -> None:
+    """Predict the next layer's routing from this layer's MoE input and install it on the
+    side stream; the next layer's apply joins before touching its cache."""
+    nxt = cache.next
+    T = x.size(0)
+    if T * k > cache.pred.numel() or x.dim() != 2 or x.dtype != torch.bfloat16 or \
+            x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        return
+    if not _prefetch_allowed():
+        return
+    dev = cache.device.index if cache.device.index is not None else \
+        torch.cuda.current_device()
+    side = _side_streams.get(dev)
+    if side is None:
+        side = _side_streams[dev] = torch.cuda.Stream(device=cache.device)
+    if nxt.ready is None:
+        nxt.ready = torch.cuda.Event()
+    main = torch.cuda.current_stream(cache.device)
+    side.wait_stream(main)              # x is written and this layer's gather is enqueued
+    x.record_stream(side)
+    with torch.cuda.stream(side):
+        pred = cache.pred[:T * k]
+        ExpertSlotCache.pregate(x, cache.next_gate, k, pred)
+        nxt.prefetch(pred)
+        nxt.ready.record(side)
+    nxt.pending = True
+
+
+def _join_prefetch(cache: ExpertSlotCache) -> None:
+    if cache.pending:
+        torch.cuda.current_stream(cache.device).wait_event(cache.ready)
+        cache.pending = False
+
+
 def _weight_names(layer) -> tuple[str, str] | None:
     for pair in _WEIGHT_PAIRS:
         if all(isinstance(getattr(layer, n, None), torch.Tensor) for n in pair):
@@ -278,6 +371,9 @@ def arm(layer, method, logger) -> bool:
         if ep_name is None:
             ids = cache.refresh(topk_ids)
             layer.global_num_experts = cache.S
+            if cache.next is not None and topk_ids.dim() == 2 and \
+                    isinstance(x, torch.Tensor):
+                _fork_prefetch(cache, x, topk_ids.size(1))
         else:
             # Expert parallel: the routing ids stay global; the layer's expert map is
             # replaced by the composed global id -> slot map for this step.
@@ -309,6 +405,7 @@ def arm(layer, method, logger) -> bool:
     # vLLM calls apply by keyword: these parameter names are part of the contract.
     def apply(layer, x, topk_weights, topk_ids, shared_experts=None,
               shared_experts_input=None):
+        _join_prefetch(cache)            # a prefetch into this layer may be in flight
         fits = cache.fits(topk_ids)
         per = 0 if fits else chunk_tokens(x, topk_ids, shared_experts)
         if debug_left[0] > 0:
@@ -346,6 +443,7 @@ def arm(layer, method, logger) -> bool:
 def _arm_model(model, logger, method_base) -> None:
     armed = declined = 0
     first = None
+    chain = []
     seen: set[int] = set()
     for _, module in model.named_modules():
         method = getattr(module, "quant_method", None)
@@ -363,6 +461,7 @@ def _arm_model(model, logger, method_base) -> None:
                 armed += 1
                 seen.add(id(method))
                 first = first or module._expert_cache
+                chain.append((module, module._expert_cache))
             else:
                 declined += 1
         except Exception as e:   # never break serving: the layer keeps the stock path
@@ -376,6 +475,9 @@ def _arm_model(model, logger, method_base) -> None:
     logger.info("expert-cache %s active on %d MoE layer(s) (%d declined): %d/%d experts "
                 "resident, mirroring %s, policy=%s", __version__, armed, declined, first.S,
                 first.E, "+".join(first.names), settings.policy)
+    if settings.prefetch:
+        logger.info("expert-cache: next-layer prefetch linked %d of %d layer pairs",
+                    _link_prefetch(chain, logger), max(len(chain) - 1, 0))
 
 
 def install(logger) -> bool:

@@ -87,6 +87,17 @@ class ExpertSlotCache:
         self.miss_total = (torch.zeros((1,), dtype=torch.int64, device=dev)
                            if settings.stats else None)
 
+        # Next-layer prefetch wiring (set by the arming code when EXPERT_CACHE_PREFETCH=1):
+        # the next armed layer's cache and router weight, a buffer for the predicted ids,
+        # and this layer's own in-flight marker (event on the side stream + flag).
+        self.next: ExpertSlotCache | None = None
+        self.next_gate: torch.Tensor | None = None
+        self.pred: torch.Tensor | None = None
+        self.ready = None
+        self.pending = False
+        self.prefetch_total = (torch.zeros((1,), dtype=torch.int64, device=dev)
+                               if settings.stats else None)
+
         self.policy = settings.policy_code
         self.decay = settings.decay
         self.chunks = settings.chunks
@@ -163,11 +174,40 @@ class ExpertSlotCache:
         self._gather(h, stream)
         return out
 
+    def prefetch(self, pred_ids: torch.Tensor) -> None:
+        """Install the predicted experts that are missing (``expert_cache_prefetch``, then
+        the gather) on the current stream.  ``pred_ids``: int32, contiguous, on device.
+        The layer's own next step still installs whatever it routes, so a wrong
+        prediction costs transfers, never results."""
+        h = lib()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+        mk = pred_ids.numel()
+        rc = h.expert_cache_prefetch(_ptr(pred_ids), mk, self.E, self.S, min(self.E, mk),
+                                     self.S, *self._state(), self.policy, stream)
+        if rc != 0:
+            raise RuntimeError(f"expert_cache_prefetch failed rc={rc}")
+        if self.prefetch_total is not None:
+            self.prefetch_total.add_(self.n_miss)
+        self._gather(h, stream)
+
+    @staticmethod
+    def pregate(x: torch.Tensor, gate_w: torch.Tensor, k: int, out: torch.Tensor) -> None:
+        """``out[t*k + r]`` = the r-th best expert of token t under router ``gate_w``
+        (``expert_cache_pregate``; bf16 x rows with unit inner stride)."""
+        h = lib()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+        rc = h.expert_cache_pregate(_ptr(x), x.size(0), x.stride(0), x.size(1), _ptr(gate_w),
+                                    gate_w.size(0), k, _ptr(out), stream)
+        if rc != 0:
+            raise RuntimeError(f"expert_cache_pregate failed rc={rc}")
+
     def stats(self) -> dict:
         """Host snapshot of the counters (synchronises; call outside the hot path)."""
         out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item())}
         if self.miss_total is not None:
             out["installs"] = int(self.miss_total.item())
+            if self.prefetch_total is not None:
+                out["prefetch_installs"] = int(self.prefetch_total.item())
             out["bytes_per_install"] = sum(_bytes_per_expert(getattr(self.owner, n).data)
                                            for n in self.names)
         return out
