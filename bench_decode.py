@@ -178,6 +178,7 @@ def cache_stats_on_worker(worker) -> list:
             st["mirrored"] = {n: list(c.slots[n].shape) for n in c.names}
             st["bound"] = sorted(c.bound)
             st["method"] = type(m.quant_method).__name__
+            st["prefetch_linked"] = c.next is not None
             out.append(st)
     return out
 
@@ -242,6 +243,7 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
     env["EXPERT_CACHE_POLICY"] = args.policy
     env["EXPERT_CACHE_STATS"] = "1" if args.stats else "0"
     env.pop("EXPERT_CACHE_SPLIT_WIDE", None)
+    env["EXPERT_CACHE_PREFETCH"] = "1" if mode.get("prefetch") else "0"
     if mode.get("split"):
         env["EXPERT_CACHE_SPLIT_WIDE"] = str(mode["split"])
     if args.deterministic:
@@ -338,11 +340,17 @@ def child(mode: dict, a) -> None:
             cache = {"armed_layers": len(layers), "layer_steps": steps,
                      "mirrored": layers[0]["mirrored"], "bound": layers[0]["bound"],
                      "method": layers[0]["method"]}
+            cache["prefetch_linked"] = sum(bool(x.get("prefetch_linked")) for x in layers)
             if "installs" in layers[0]:
                 cache.update(installs=installs,
                              installs_per_layer_step=round(installs / max(steps, 1), 4),
                              bytes_per_install=layers[0].get("bytes_per_install"))
+            if "prefetch_installs" in layers[0]:
+                pf = sum(x["prefetch_installs"] for x in layers)
+                cache.update(prefetch_installs=pf,
+                             prefetch_installs_per_layer_step=round(pf / max(steps, 1), 4))
     out = {"mode": mode["name"], "slots": mode.get("slots"), "split_wide": mode.get("split", 0),
+           "prefetch": bool(mode.get("prefetch")),
            "offload": bool(mode.get("offload")),
            "tp": a.tp, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
            "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
@@ -367,6 +375,8 @@ def main(argv=None):
                     default="int8-experts")
     ap.add_argument("--offload-gb", type=float, default=64.0)
     ap.add_argument("--no-offload-baseline", action="store_true")
+    ap.add_argument("--no-resident", action="store_true",
+                    help="skip the resident mode: the first mode run is the comparison base")
     ap.add_argument("--stats", action="store_true",
                     help="EXPERT_CACHE_STATS=1: count installs (adds one small kernel per "
                          "layer-step, so keep it off for timing)")
@@ -389,6 +399,9 @@ def main(argv=None):
     ap.add_argument("--split-wide", type=int, nargs="*", default=[],
                     help="EXPERT_CACHE_SPLIT_WIDE values: every slot count runs once per "
                          "value (0 = the reference's read-through of wide steps)")
+    ap.add_argument("--prefetch", type=int, nargs="*", default=[],
+                    help="EXPERT_CACHE_PREFETCH values (0/1): every slot count runs once "
+                         "per value")
     ap.add_argument("--parity-batch", action="store_true",
                     help="greedy parity run over the whole batch instead of its first prompt")
     ap.add_argument("--mode-timeout", type=int, default=1200)
@@ -405,14 +418,15 @@ def main(argv=None):
     model_dir, site = tmp / "model", tmp / "site"
     write_model_dir(model_dir, a.layers, a.prompt + a.gen + 16, a.quant, a.arch)
     write_plugin_site(site)
-    modes = [{"name": "resident"}]
+    modes = [] if a.no_resident else [{"name": "resident"}]
     if a.control:
         modes.append({"name": "resident-again"})   # the engine's own run-to-run spread
     if not a.no_offload_baseline:
         modes.append({"name": "offload", "offload": True, "offload_gb": a.offload_gb})
-    modes += [{"name": f"slots{s}" + (f"-split{v}" if v else ""), "slots": s, "split": v,
-               "offload": True, "offload_gb": a.offload_gb}
-              for s in a.slots for v in (a.split_wide or [0])]
+    modes += [{"name": f"slots{s}" + (f"-split{v}" if v else "") + ("-prefetch" if f else ""),
+               "slots": s, "split": v, "prefetch": f, "offload": True,
+               "offload_gb": a.offload_gb}
+              for s in a.slots for v in (a.split_wide or [0]) for f in (a.prefetch or [0])]
     results = []
     base = None
     for m in modes:

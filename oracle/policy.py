@@ -207,13 +207,16 @@ def prefetch(st: CacheState, ids, max_distinct: int, max_inserts: int,
     """``expert_cache_prefetch``: install the predicted experts that are missing, with the
     victim order and install rules of :func:`manage`, and change nothing else -- ``step``
     does not advance, hits keep their priority, no ageing.  New slots take priority
-    ``step`` (LRU) or 1 (LFU).  The reference has no prefetch (its README.md:392-394
-    names it as unexplored); the rules are the manage rules above minus the step's own
-    bookkeeping."""
+    ``step`` (LRU) or 1 (LFU).  Slots holding an expert the previous call routed (the
+    ``routed`` flags on entry) are parked like the predicted ones: a speculative install
+    never evicts the last step's working set.  ``routed`` is left holding the predicted
+    flags.  The reference has no prefetch (its README.md:392-394 names it as
+    unexplored); the rules are the manage rules above minus the step's own bookkeeping."""
     E, S = st.E, st.S
     ids = np.asarray(ids).reshape(-1).astype(np.int64)
     now = int(st.step[0])
     st.n_miss[0] = 0
+    previous = st.routed.copy()
     st.routed[:] = 0
     st.routed[ids[(ids >= 0) & (ids < E)]] = 1
     routed = np.flatnonzero(st.routed)
@@ -227,7 +230,7 @@ def prefetch(st: CacheState, ids, max_distinct: int, max_inserts: int,
         st.miss[2 * j] = missing[j]
     se, stamp = st.slot_expert, st.slot_stamp
     evictable = [i for i in range(S)
-                 if se[i] < 0 or se[i] >= E or not st.routed[se[i]]]
+                 if se[i] < 0 or se[i] >= E or not (st.routed[se[i]] or previous[se[i]])]
     evictable.sort(key=lambda i: (int(stamp[i]), i))
     fresh = now if policy == LRU else 1
     out = []

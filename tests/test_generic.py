@@ -587,7 +587,8 @@ def armed_chain(layers):
     return chain
 
 
-def test_prefetch_links_consecutive_layers_with_usable_routers():
+def test_prefetch_links_consecutive_layers_with_usable_routers(monkeypatch):
+    monkeypatch.setenv("EXPERT_CACHE_PREFETCH", "3")
     bad_dtype = gated(torch.randn(E, 64))                        # fp32 router
     bad_width = gated(torch.randn(E, 60).to(torch.bfloat16))     # hidden % 8 != 0
     layers = [gated(), gated(), bad_dtype, gated(), bad_width]
@@ -598,6 +599,7 @@ def test_prefetch_links_consecutive_layers_with_usable_routers():
     assert caches[0].next is caches[1]
     assert caches[0].next_gate is layers[1].runner.gate.weight
     assert caches[0].pred.shape == (S,) and caches[0].pred.dtype == torch.int32
+    assert caches[0].prefetch_top == 3
     assert caches[1].next is None                 # the next router is fp32
     assert caches[2].next is caches[3]
     assert caches[3].next is None and caches[4].next is None

@@ -210,17 +210,19 @@ def test_prefetch_known_answer():
     ``step`` (LRU)."""
     st = policy.CacheState(8, 3)
     policy.manage(st, [1, 2], 8, 3, policy.LRU, 0)            # step 1: 1->s0, 2->s1
-    policy.manage(st, [2], 8, 3, policy.LRU, 0)               # step 2: 2 refreshed
-    assert st.slot_stamp.tolist() == [1, 2, 0]
+    policy.manage(st, [3], 8, 3, policy.LRU, 0)               # step 2: 3->s2
+    assert st.slot_stamp.tolist() == [1, 1, 2]
     pairs = policy.prefetch(st, [2, 5, 6], 8, 3, policy.LRU)
-    # victims: empty slot 2 (stamp 0), then slot 0 (expert 1, stamp 1); slot 1 is parked
-    assert pairs == [(5, 2), (6, 0)]
+    # slot 1 holds predicted expert 2 and slot 2 the last step's expert 3: both parked,
+    # so only slot 0 (expert 1) can take a prediction -- 5, the lower missing id
+    assert pairs == [(5, 0)]
     assert int(st.step[0]) == 2
-    assert st.slot_stamp.tolist() == [2, 2, 2]
+    assert st.slot_stamp.tolist() == [2, 1, 2]
     assert st.table[1] == -1 and st.map_cold[1] == 1 and st.table[2] == 1
-    assert int(st.n_miss[0]) == 2
-    # a real step afterwards sees the prefetched experts as hits
-    assert policy.manage(st, [5, 6], 8, 3, policy.LRU, 0) == []
+    assert int(st.n_miss[0]) == 1 and st.miss[2] == 6          # 6 listed, not installed
+    assert st.routed.tolist() == [0, 0, 1, 0, 0, 1, 1, 0]     # the predicted flags
+    # a real step afterwards sees the prefetched expert as a hit
+    assert policy.manage(st, [5, 3], 8, 3, policy.LRU, 0) == []
 
 
 def test_prefetch_lfu_keeps_counts_and_skips_ageing():

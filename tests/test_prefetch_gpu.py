@@ -8,8 +8,8 @@ oracle, and two chained layers through vLLM's own fused-MoE kernel.
 * Two armed W8A8 int8 layers (vLLM's Triton ``fused_experts``), the second's router on
   ``layer.runner.gate``: with prefetch on, every output equals the stock kernel's bit for
   bit, eagerly and replayed from a captured CUDA graph (the side-stream fork and join are
-  recorded in the graph); the prefetch installs experts and the second layer's own steps
-  install fewer than without it.
+  recorded in the graph); the prefetch installs experts (never over the previous step's
+  working set) and the second layer's own steps install fewer than without it.
 """
 
 from __future__ import annotations
@@ -168,7 +168,7 @@ def route(layer, x):
 def build_pair(vllm_moe, monkeypatch, prefetch: bool):
     monkeypatch.setenv("EXPERT_CACHE_SLOTS", str(S2))
     monkeypatch.setenv("EXPERT_CACHE_STATS", "1")
-    monkeypatch.setenv("EXPERT_CACHE_PREFETCH", "1" if prefetch else "0")
+    monkeypatch.setenv("EXPERT_CACHE_PREFETCH", str(K2) if prefetch else "0")
     from vllm_expert_cache.backends import generic
     layers = [GatedLayer(seed=11), GatedLayer(seed=12)]
     methods = [Int8Method(ly, *vllm_moe) for ly in layers]
@@ -185,7 +185,7 @@ def build_pair(vllm_moe, monkeypatch, prefetch: bool):
 def drive(layers, methods, stocks, steps, seed):
     rng = torch.Generator().manual_seed(seed)
     for step in range(steps):
-        x = torch.randn(2, H2, generator=rng).to(torch.bfloat16).cuda()   # 2 x 4 ids = S
+        x = torch.randn(1, H2, generator=rng).to(torch.bfloat16).cuda()   # 4 ids of 8 slots
         for i, (ly, m, stock) in enumerate(zip(layers, methods, stocks)):
             w, ids = route(ly, x)
             got = m.apply(ly, x, w, ids)
@@ -214,8 +214,8 @@ def test_prefetch_keeps_outputs_exact_and_saves_installs(vllm_moe, monkeypatch):
 def test_prefetch_inside_a_captured_graph(vllm_moe, monkeypatch):
     layers, methods, stocks = build_pair(vllm_moe, monkeypatch, prefetch=True)
     drive(layers, methods, stocks, 3, seed=2)          # warm: Triton JIT, events, streams
-    x = torch.zeros(2, H2, dtype=torch.bfloat16, device=DEV)
-    routes = [[torch.zeros(2, K2, device=DEV), torch.zeros(2, K2, dtype=torch.int32,
+    x = torch.zeros(1, H2, dtype=torch.bfloat16, device=DEV)
+    routes = [[torch.zeros(1, K2, device=DEV), torch.zeros(1, K2, dtype=torch.int32,
                                                            device=DEV)] for _ in layers]
     outs = [None, None]
 
@@ -233,7 +233,7 @@ def test_prefetch_inside_a_captured_graph(vllm_moe, monkeypatch):
         forward()
     rng = torch.Generator().manual_seed(9)
     for step in range(12):
-        xn = torch.randn(2, H2, generator=rng).to(torch.bfloat16).cuda()
+        xn = torch.randn(1, H2, generator=rng).to(torch.bfloat16).cuda()
         x.copy_(xn)
         for i, ly in enumerate(layers):
             w, ids = route(ly, xn)

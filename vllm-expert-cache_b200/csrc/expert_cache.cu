@@ -84,7 +84,8 @@ struct ManageArgs {
   int Eg;
   int* out_map;
   // Prefetch (expert_cache_prefetch): install the predicted experts that are missing and
-  // change nothing else -- no step advance, no priority refresh of hits, no ageing.
+  // change nothing else -- no step advance, no priority refresh of hits, no ageing -- and
+  // never evict a slot whose expert the previous step routed (its `routed` flags).
   int prefetch;
 };
 
@@ -161,9 +162,11 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
 
   // ---- one round of loads: step, table, slot state (ids were read by the caller) -------
   const long long now = a.step[0] + (a.prefetch ? 0 : 1);
+  // Flag bits: 1 = routed by this call's ids; 2 = routed by the previous step (prefetch
+  // only: those slots are parked, not installed).
   for (int e = t; e < E; e += NT) {
     s_tab[e] = a.table[e];
-    s_flag[e] = 0;
+    s_flag[e] = (a.prefetch && a.routed[e]) ? 2 : 0;
   }
   for (int s = t; s < S; s += NT) {
     s_se[s] = a.slot_expert[s];
@@ -172,11 +175,11 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   __syncthreads();
   if (t == 0 && !a.prefetch) a.step[0] = now;   // every thread read the old value above
 
-  // ---- routed flags (duplicates write the same 1) ---------------------------------------
-  if (my_id >= 0 && my_id < E) s_flag[my_id] = 1;
+  // ---- routed flags (every writer of an entry stores the same value) -------------------
+  if (my_id >= 0 && my_id < E) s_flag[my_id] |= 1;
   for (int i = t + NT; i < a.mk; i += NT) {
     const int e = local_expert(a, a.ids[i]);
-    if (e >= 0 && e < E) s_flag[e] = 1;
+    if (e >= 0 && e < E) s_flag[e] |= 1;
   }
   __syncthreads();
 
@@ -200,7 +203,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   int distinct = 0, n_missing = 0;
   for (int base = 0, tile = 0; base < E; base += NT, ++tile) {
     const int e = base + t;
-    const bool f = e < E && s_flag[e];
+    const bool f = e < E && (s_flag[e] & 1);
     const bool m = f && s_tab[e] < 0;
     const unsigned bf = __ballot_sync(0xffffffffu, f);
     const unsigned bm = __ballot_sync(0xffffffffu, m);
@@ -229,7 +232,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
 #pragma unroll
   for (int k = 0; k < NW; ++k) n_evict += w_evict[k];
 
-  for (int e = t; e < E; e += NT) a.routed[e] = s_flag[e];
+  for (int e = t; e < E; e += NT) a.routed[e] = s_flag[e] & 1;
 
   const bool read_through = distinct > a.max_distinct;
   const int nins = read_through ? 0 : min(n_missing, a.max_inserts);

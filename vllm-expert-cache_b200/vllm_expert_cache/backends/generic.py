@@ -233,6 +233,7 @@ def _link_prefetch(armed: list, logger) -> int:
             continue
         ci.next, ci.next_gate = cj, w
         ci.pred = torch.empty((ci.S,), dtype=torch.int32, device=ci.device)
+        ci.prefetch_top = settings.prefetch
         linked += 1
     return linked
 
@@ -252,10 +253,12 @@ def _prefetch_allowed() -> bool:
 
 
 def _fork_prefetch(cache: ExpertSlotCache, x: torch.Tensor, k: int) -> None:
-    """Predict the next layer's routing from this layer's MoE input and install it on the
-    side stream; the next layer's apply joins before touching its cache."""
+    """Predict the next layer's routing from this layer's MoE input and install its top
+    ``prefetch_top`` experts per token on the side stream; the next layer's apply joins
+    before touching its cache."""
     nxt = cache.next
     T = x.size(0)
+    k = min(k, cache.prefetch_top)
     if T * k > cache.pred.numel() or x.dim() != 2 or x.dtype != torch.bfloat16 or \
             x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
         return

@@ -93,6 +93,7 @@ class ExpertSlotCache:
         self.next: ExpertSlotCache | None = None
         self.next_gate: torch.Tensor | None = None
         self.pred: torch.Tensor | None = None
+        self.prefetch_top = 0           # predictions per token to prefetch
         self.ready = None
         self.pending = False
         self.prefetch_total = (torch.zeros((1,), dtype=torch.int64, device=dev)

@@ -24,10 +24,10 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
   EXPERT_CACHE_EP         0       '1' caches expert-parallel layers (standard activation
                                   format, vLLM expert_map) instead of refusing them as the
                                   reference does (new, off by default)
-  EXPERT_CACHE_PREFETCH   0       '1' predicts each armed layer's routing from the
-                                  previous layer's MoE input and installs the predicted
-                                  experts on a side stream while that layer computes
-                                  (new, off by default)
+  EXPERT_CACHE_PREFETCH   0       N > 0 predicts each armed layer's routing from the
+                                  previous layer's MoE input and installs the top N
+                                  predicted experts per token on a side stream while that
+                                  layer computes (new, off by default)
 
 ``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
 """
@@ -94,8 +94,8 @@ class Settings:
         return _env("EXPERT_CACHE_EP", "0") == "1"
 
     @property
-    def prefetch(self) -> bool:
-        return _env("EXPERT_CACHE_PREFETCH", "0") == "1"
+    def prefetch(self) -> int:
+        return max(0, int(_env("EXPERT_CACHE_PREFETCH", "0") or 0))
 
     def slots_for(self, num_experts: int) -> int:
         want = self.slots
