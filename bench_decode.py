@@ -405,7 +405,8 @@ def main(argv=None):
     ap.add_argument("--parity-batch", action="store_true",
                     help="greedy parity run over the whole batch instead of its first prompt")
     ap.add_argument("--mode-timeout", type=int, default=1200)
-    ap.add_argument("--logdir", default="gpurun_out")
+    ap.add_argument("--logdir", default=str(Path(tempfile.gettempdir()) / "expert_cache_decode"),
+                    help="per-mode engine logs")
     ap.add_argument("--child", default=None)
     ap.add_argument("--model", default=None)
     a = ap.parse_args(argv)

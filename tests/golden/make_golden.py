@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout is readable:
 
-    python tests/golden/make_golden.py [--ref PATH]      (default PATH: /root/reference)
+    python tests/golden/make_golden.py --ref PATH        (PATH: the reference checkout)
 
 What it runs from the reference, extracted by ``ast`` so the modules' import-time side
 effects (a ``ctypes.CDLL`` of the HIP library, tests/test_policy.py:20-22) never execute:
@@ -143,7 +143,7 @@ def suite_traces():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the reference checkout")
     args = ap.parse_args()
     ref = Path(args.ref)
     env = {"np": np, "POLICY": 0, "DECAY": 64}
