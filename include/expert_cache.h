@@ -115,6 +115,9 @@ EXPERT_CACHE_API int expert_cache_manage_ep(
  *   - `step` does not advance;
  *   - hits keep their priority;
  *   - no ageing runs.
+ * Slots whose expert is flagged in `routed` on entry are parked like predicted ones, so
+ * when the call before this one was the layer's own step, its experts are never evicted.
+ * `routed` is left holding the predicted flags.
  *
  * A wrong prediction therefore costs transfers and evictions, never results: the
  * layer's own step still installs whatever it routes.

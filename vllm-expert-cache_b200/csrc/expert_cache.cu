@@ -85,7 +85,8 @@ struct ManageArgs {
   int* out_map;
   // Prefetch (expert_cache_prefetch): install the predicted experts that are missing and
   // change nothing else -- no step advance, no priority refresh of hits, no ageing -- and
-  // never evict a slot whose expert the previous step routed (its `routed` flags).
+  // never evict a slot whose expert is flagged in `routed` on entry (the previous call's
+  // routing: the layer's own step, when prefetches and steps alternate).
   int prefetch;
 };
 

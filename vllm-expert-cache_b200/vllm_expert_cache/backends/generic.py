@@ -368,13 +368,16 @@ def arm(layer, method, logger) -> bool:
             split_max = 0
     split = [split_max]
 
-    def cached(layer, x, topk_weights, topk_ids, shared_experts, shared_experts_input):
+    def cached(layer, x, topk_weights, topk_ids, shared_experts, shared_experts_input,
+               fork=True):
         experts = method.moe_kernel.fused_experts
         saved = (experts.quant_config, method.moe_quant_config, layer.global_num_experts)
         if ep_name is None:
             ids = cache.refresh(topk_ids)
             layer.global_num_experts = cache.S
-            if cache.next is not None and topk_ids.dim() == 2 and \
+            # one prefetch per real step: a prefetch parks the experts flagged by the call
+            # before it, which must be this layer's step, not another prefetch
+            if fork and cache.next is not None and topk_ids.dim() == 2 and \
                     isinstance(x, torch.Tensor):
                 _fork_prefetch(cache, x, topk_ids.size(1))
         else:
@@ -428,7 +431,7 @@ def arm(layer, method, logger) -> bool:
         outs = []
         for lo in range(0, topk_ids.size(0), per):
             out = cached(layer, x[lo:lo + per], topk_weights[lo:lo + per],
-                         topk_ids[lo:lo + per], None, None)
+                         topk_ids[lo:lo + per], None, None, fork=False)
             if not isinstance(out, torch.Tensor):
                 logger.warning("expert-cache: %s apply returned %s, not a tensor; wide "
                                "steps read through from now on", kind, type(out).__name__)
