@@ -222,7 +222,7 @@ class Layer:
 
     def __init__(self, S, seed, device, policy_code, decay, chunks, lanes):
         import torch
-        from vllm_expert_cache import synthetic
+        import synthetic
         self.torch = torch
         self.device = device
         self.E, self.S = E_EXPERTS, S
@@ -390,7 +390,7 @@ def kernel_pass(layer, trace_dev, out_dev, W, K):
 def e2e_pass(layer, trace, W, K, tokens):
     """Through the public per-layer API (ExpertSlotCache.refresh) with host buffers."""
     import torch
-    from vllm_expert_cache import synthetic
+    import synthetic
     from vllm_expert_cache.cache import ExpertSlotCache
 
     class Owner(torch.nn.Module):
@@ -468,7 +468,7 @@ def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64, E=E_EXPERTS, t
     ``E`` / ``S`` / the caps select another workload (the reference's timing shape)."""
     import torch
     from vllm_expert_cache import _lib
-    from vllm_expert_cache.synthetic import sticky_zipf_trace
+    from synthetic import sticky_zipf_trace
     h = _lib.lib()
     if trace is None:
         trace = sticky_zipf_trace(seed, steps=steps, E=E)

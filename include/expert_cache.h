@@ -4,11 +4,16 @@
  * argument meaning and return codes, with cudaStream_t in place of hipStream_t.  Every
  * pointer is device-accessible memory owned by the caller (PyTorch tensors passed as raw
  * pointers; gather sources may be UVA views of pinned host memory).  Every call only
- * enqueues work on `stream`: no host synchronisation, no allocation, no library state
- * beyond per-device kernel attributes, so every call is legal inside CUDA-graph capture.
+ * enqueues work on `stream`: no host synchronisation and no allocation.  The library keeps
+ * per-device kernel attributes and SM counts, looked up on a device's first call.
  *
- * Return codes: 0 = enqueued; -1 = arguments refused (nothing enqueued); any other value
- * is the cudaError_t of the launch.
+ * One exception holds device memory of its own: expert_cache_manage_remap_noalloc writes
+ * into a library-owned device array, so its first call on each device (which looks up that
+ * array's address) must come before any stream capture on that device.
+ *
+ * Return codes: 0 = enqueued; -1 = arguments refused (nothing enqueued); -2 = E above
+ * EXPERT_CACHE_NOALLOC_MAX_EXPERTS (expert_cache_manage_remap_noalloc only); any other
+ * value is the cudaError_t of the launch or of a first-call attribute lookup.
  */
 #ifndef EXPERT_CACHE_H
 #define EXPERT_CACHE_H

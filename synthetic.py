@@ -1,7 +1,9 @@
-"""Seeded synthetic inputs with the benchmark shapes: routing traces and W8A8 expert slabs.
+"""Seeded synthetic inputs for the benchmarks and tests: routing traces and W8A8 slabs.
 
-No real checkpoint or captured routing is available, so the benchmarks and tests use
-these stand-ins, sized and distributed like the workloads the cache is measured on:
+Benchmark and test helper only: it sits beside ``bench.py`` and is not part of the
+installed ``vllm_expert_cache`` plugin.  No real checkpoint or captured routing is
+available, so the benchmarks and tests use these stand-ins, sized and distributed like
+the workloads the cache is measured on:
 
 * :func:`sticky_zipf_trace` -- decode routing with temporal locality: 8 distinct experts
   per token; each position keeps the previous token's expert with probability ``p_keep``,

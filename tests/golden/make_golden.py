@@ -33,7 +33,7 @@ sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REPO / "vllm-expert-cache_b200"))
 
 from oracle import hashing  # noqa: E402
-from vllm_expert_cache.synthetic import sticky_zipf_trace  # noqa: E402
+from synthetic import sticky_zipf_trace  # noqa: E402
 
 OUT = Path(__file__).resolve().parent / "golden.npz"
 

@@ -6,7 +6,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from vllm_expert_cache.synthetic import sticky_zipf_trace
+from synthetic import sticky_zipf_trace
 
 # The twelve published miss counts: README.md:179-184 of the reference, (LRU, LFU).
 PUBLISHED = {

@@ -78,11 +78,11 @@ def compare_state(ds_host: dict, st: CacheState, nins: int, tag: str) -> None:
 
 
 def device_ptr_of_pinned(host: torch.Tensor) -> int:
-    from vllm_expert_cache.synthetic import host_device_pointer
+    from synthetic import host_device_pointer
     return host_device_pointer(host)
 
 
 def uva_view(host: torch.Tensor) -> torch.Tensor:
     """A CUDA tensor aliasing pinned host memory (reads cross the host link)."""
-    from vllm_expert_cache.synthetic import uva_view as _view
+    from synthetic import uva_view as _view
     return _view(host, DEV)

@@ -16,7 +16,7 @@ import torch
 from gpu_util import DEV, uva_view
 from oracle import policy
 from vllm_expert_cache.cache import ExpertSlotCache
-from vllm_expert_cache.synthetic import qwen3_30b_a3b_experts, sticky_zipf_trace
+from synthetic import qwen3_30b_a3b_experts, sticky_zipf_trace
 
 pytestmark = pytest.mark.gpu
 

@@ -72,7 +72,7 @@ def test_six_buffer_byte_identity_drive(h):
 
 @pytest.mark.parametrize("chunks,lanes", [(16, 64), (1, 1), (3, 5), (148, 2), (64, 64)])
 def test_qwen3_w8a8_slab_any_grid(h, chunks, lanes):
-    from vllm_expert_cache.synthetic import bytes_per_expert, qwen3_30b_a3b_experts
+    from synthetic import bytes_per_expert, qwen3_30b_a3b_experts
     E, S = 12, 8
     ex = qwen3_30b_a3b_experts(E=E, seed=5)
     names = list(ex)

@@ -550,6 +550,18 @@ def test_ep_refusals(monkeypatch, setup, reason):
     assert not ok and log.said(reason), log.msgs
 
 
+@pytest.mark.parametrize("attr,value", [("eplb_state", object()), ("enable_eplb", True)])
+def test_eplb_layer_is_refused(monkeypatch, attr, value):
+    # EPLB moves experts between ranks by rewriting the weight rows and expert_map in
+    # place; a cache keyed by the old placement would serve the wrong expert's rows.
+    monkeypatch.setenv("EXPERT_CACHE_EP", "1")
+    layer = EPExperts()
+    setattr(layer, attr, value)
+    ok, log = arm(layer, ep_method(layer))
+    assert not ok and log.said("EPLB"), log.msgs
+    assert getattr(layer, "_expert_cache", None) is None
+
+
 def test_ep_without_a_map_is_refused(monkeypatch):
     monkeypatch.setenv("EXPERT_CACHE_EP", "1")
     layer = RoutedExperts()
@@ -632,3 +644,37 @@ def test_prefetch_is_skipped_while_vllm_captures_piecewise(monkeypatch):
         ctx = type("Ctx", (), {"cudagraph_runtime_mode": type("M", (), {"name": name})()})()
         monkeypatch.setattr(fc, "get_forward_context", lambda c=ctx: c)
         assert generic._prefetch_allowed() == allowed, name
+
+
+def test_prefetch_waits_for_a_full_step_of_the_next_layer(monkeypatch):
+    # A prefetch parks the experts flagged in the next layer's `routed`; those must be the
+    # next layer's last full cached step, never a prefetch's predictions, a split chunk's
+    # subset or a stale state left by a read-through.
+    monkeypatch.setenv("EXPERT_CACHE_PREFETCH", "2")
+    monkeypatch.setenv("EXPERT_CACHE_SPLIT_WIDE", "4")
+    nxt = gated()
+    m = RowMethod(nxt)
+    assert arm(nxt, m)[0]
+    cache = nxt._expert_cache
+    cache.refresh = lambda ids: ids + 100
+    first = gated()
+    assert arm(first, QuantMethod(first))[0]
+    assert generic._link_prefetch([(first, first._expert_cache), (nxt, cache)], Log()) == 1
+    x = torch.randn(1, 64).to(torch.bfloat16)
+
+    def forks():    # a fork that gets past the check would need CUDA streams here
+        try:
+            generic._fork_prefetch(first._expert_cache, x, 2)
+        except (RuntimeError, AssertionError, AttributeError):
+            return True
+        return False
+
+    assert not cache.routed_is_step and not forks()        # never stepped yet
+    m.apply(nxt, *wide_step(1))                             # a full cached step
+    assert cache.routed_is_step and forks()
+    m.apply(nxt, *wide_step(5))                             # split into chunks
+    assert not cache.routed_is_step and not forks()
+    m.apply(nxt, *wide_step(1))
+    assert cache.routed_is_step
+    m.apply(nxt, *wide_step(12))                            # too wide: reads through
+    assert not cache.routed_is_step and not forks()

@@ -189,7 +189,7 @@ def test_cuda_graph_replay(h):
     # capture does not execute: the state is still the initial one
     torch.cuda.synchronize()
     np.testing.assert_array_equal(ds.step.cpu().numpy(), [0])
-    from vllm_expert_cache.synthetic import sticky_zipf_trace
+    from synthetic import sticky_zipf_trace
     trace = sticky_zipf_trace(9, steps=200, E=E)
     for t in range(200):
         ids_buf.copy_(torch.from_numpy(trace[t]))
@@ -206,7 +206,7 @@ def test_two_replicas_evolve_identically(h):
     """Tensor-parallel ranks see the same routing: their caches must stay identical."""
     E, S = 128, 64
     a, b = DeviceState(policy.CacheState(E, S)), DeviceState(policy.CacheState(E, S))
-    from vllm_expert_cache.synthetic import sticky_zipf_trace
+    from synthetic import sticky_zipf_trace
     tr = torch.from_numpy(sticky_zipf_trace(2, steps=300)).to(DEV)
     side = torch.cuda.Stream()
     for t in range(300):

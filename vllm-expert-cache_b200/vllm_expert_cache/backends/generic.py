@@ -155,6 +155,12 @@ def _decline(layer, method, num_experts: int) -> str | None:
         return "method has no moe_kernel (legacy non-modular path)"
     if getattr(kernel, "fused_experts", None) is None:
         return "moe_kernel exposes no fused_experts to rebind"
+    if getattr(layer, "eplb_state", None) is not None or getattr(layer, "enable_eplb", False):
+        # vLLM's expert load balancer rewrites the layer's expert rows and expert_map in
+        # place between steps (rearrange_expert_weights_inplace); the cache's table and
+        # slot contents would stay keyed by the old placement and serve wrong experts.
+        return ("expert load balancing (EPLB) rearranges the expert weights between "
+                "steps")
     if getattr(layer, "expert_map", None) is not None:
         if not settings.ep:
             return "expert parallelism active (layer.expert_map is set)"
@@ -257,6 +263,11 @@ def _fork_prefetch(cache: ExpertSlotCache, x: torch.Tensor, k: int) -> None:
     ``prefetch_top`` experts per token on the side stream; the next layer's apply joins
     before touching its cache."""
     nxt = cache.next
+    if not nxt.routed_is_step:
+        # The next layer's `routed` does not hold its last real step (its last call was a
+        # prefetch, a split chunk or a read-through), so a prefetch could evict experts
+        # that step needs: skip until the next layer has run a full cached step again.
+        return
     T = x.size(0)
     k = min(k, cache.prefetch_top)
     if T * k > cache.pred.numel() or x.dim() != 2 or x.dtype != torch.bfloat16 or \
@@ -374,6 +385,7 @@ def arm(layer, method, logger) -> bool:
         saved = (experts.quant_config, method.moe_quant_config, layer.global_num_experts)
         if ep_name is None:
             ids = cache.refresh(topk_ids)
+            cache.routed_is_step = fork       # a split chunk flags only its own tokens
             layer.global_num_experts = cache.S
             # one prefetch per real step: a prefetch parks the experts flagged by the call
             # before it, which must be this layer's step, not another prefetch
@@ -424,6 +436,7 @@ def arm(layer, method, logger) -> bool:
             return cached(layer, x, topk_weights, topk_ids, shared_experts,
                           shared_experts_input)
         if not per:
+            cache.routed_is_step = False      # read through: `routed` is not this step's
             return stock_apply(layer, x, topk_weights, topk_ids, shared_experts,
                                shared_experts_input)
         # Each chunk is an ordinary cached step over consecutive tokens; a token's output

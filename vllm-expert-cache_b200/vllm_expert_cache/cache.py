@@ -96,6 +96,11 @@ class ExpertSlotCache:
         self.prefetch_top = 0           # predictions per token to prefetch
         self.ready = None
         self.pending = False
+        # True while `routed` holds this layer's last full cached step (set by the arming
+        # code after such a step; cleared by a prefetch, a split chunk or a read-through).
+        # A prefetch parks the experts flagged in `routed`, so it is only issued when this
+        # holds.
+        self.routed_is_step = False
         self.prefetch_total = (torch.zeros((1,), dtype=torch.int64, device=dev)
                                if settings.stats else None)
 
@@ -189,6 +194,7 @@ class ExpertSlotCache:
             raise RuntimeError(f"expert_cache_prefetch failed rc={rc}")
         if self.prefetch_total is not None:
             self.prefetch_total.add_(self.n_miss)
+        self.routed_is_step = False       # `routed` now holds the predicted flags
         self._gather(h, stream)
 
     @staticmethod
