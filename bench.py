@@ -4,9 +4,11 @@
 Workload (one MoE layer, Qwen3-30B-A3B W8A8 shapes, TP1): 128 experts of 4,732,928 B
 (w13 int8 [1536,2048], w2 int8 [2048,768], fp32 per-row scales) in pinned host memory,
 S device slots, a decode step of ``tokens`` x top-8 routing ids carrying exactly
-``misses`` experts that are not resident.  One step = one ``expert_cache_manage_remap``
-launch (policy + victim choice + remap) followed by one ``expert_cache_gather`` launch
-(the missing slabs over the host link into their slots).
+``misses`` experts that are not resident.  One step = one ``expert_cache_step`` launch:
+policy + victim choice + remap in its first CTA, then the missing slabs over the host
+link into their slots by all its CTAs (the path ``ExpertSlotCache.refresh`` takes).  The
+two-launch form of the same step (``expert_cache_manage_remap`` + ``expert_cache_gather``)
+is timed beside it.
 
 Forced misses are planned with the product kernel itself in an untimed pass (host reads
 of the table choose ``misses`` absent and ``8*tokens - misses`` resident experts per
@@ -16,9 +18,12 @@ determinism makes every replay install exactly the planned experts (checked).
 Printed (rank 0, one JSON line): ``value`` = gathered bytes / device time of the K timed
 steps with inputs resident (max over ranks, summed over ranks); ``e2e`` = the same bytes
 through ``ExpertSlotCache.refresh`` with the routing ids copied in from pinned host
-memory and the slot ids copied back every step; ``roofline`` for the gather kernel
-against the pinned host-to-device copy-engine bandwidth measured in the same run;
-``cpu_baseline`` = the CPU oracle (policy step + memcpy of the slabs) on one host core.
+memory and the slot ids copied back every step; ``roofline`` for the step kernel against
+the pinned host-to-device copy-engine bandwidth measured in the same run with every rank
+copying at once (the host link each rank really has when all N gather together);
+``cpu_baseline`` = the CPU oracle (policy step + memcpy of the slabs) on one host core
+for at least two seconds; at N=1 also ``decode`` (bench_decode.py: end-to-end decode
+through vLLM, config 3, resident vs cached vs vLLM's uncached offload).
 
 ``--impl reference`` runs the CPU restatement of the reference's policy path on all
 usable host cores (policy step + host memcpy of the same slabs into host slot buffers),
@@ -46,11 +51,14 @@ METRIC = "miss-gather GB/s vs host-link peak"
 E_EXPERTS = 128
 TOP_K = 8
 L2_BYTES = 126 * 1024 * 1024
-# dram__bytes_read.sum + dram__bytes_write.sum of one gather launch at the default
-# workload (4 misses), from the ncu capture summarised in profiles/gather_kernel_s64_m4.txt:
-# 9,728 B read + 0 B written.  The host-memory reads are not DRAM traffic and the slot
-# writes are still in L2 when the launch ends.
-GATHER_DRAM_BYTES = 9728
+# dram__bytes_read.sum + dram__bytes_write.sum of one step-kernel launch at the default
+# workload (S=64, 4 misses), from the ncu capture summarised in
+# profiles/step_kernel_s64_m4.txt.  The host-memory reads are not DRAM traffic and the
+# slot writes are still in L2 when the launch ends; printed with its source.
+STEP_DRAM_BYTES = None
+STEP_DRAM_SOURCE = "profiles/step_kernel_s64_m4.txt (ncu, one launch)"
+# Layer-steps each worker of the reference arm times (K steps of R layer-steps).
+REF_LAYER_STEPS = 600
 
 
 def parse(argv=None):
@@ -71,6 +79,15 @@ def parse(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-policy-sim", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the end-to-end vLLM decode leg (N=1 only)")
+    ap.add_argument("--decode-gen", type=int, default=128)
+    ap.add_argument("--decode-slots", type=int, default=64)
+    ap.add_argument("--decode-budget-s", type=float, default=720,
+                    help="wall-time budget of the decode leg: modes not started by then are "
+                         "reported as skipped")
+    ap.add_argument("--cpu-seconds", type=float, default=2.0,
+                    help="minimum duration of the one-core CPU baseline")
     a = ap.parse_args(argv)
     if a.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -112,6 +129,9 @@ class Dist:
 
     def sum(self, x: float, device=None) -> float:
         return self._reduce(x, "sum", device)
+
+    def min(self, x: float, device=None) -> float:
+        return -self._reduce(-x, "max", device)
 
     def _reduce(self, x, op, device):
         if not self.pg:
@@ -196,8 +216,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 # workload
 
-def h2d_peak_gbs(device, nbytes=512 << 20, reps=10):
-    """Pinned host -> device copy-engine bandwidth (the host-link denominator)."""
+def h2d_peaks(device, dist, nbytes=512 << 20, reps=8):
+    """Pinned host -> device copy-engine bandwidth, the host-link denominator.
+
+    Returns ``(alone, concurrent)``: ``alone`` = this rank's best copy while the other
+    ranks wait (ranks take turns); ``concurrent`` = every rank copying at once after a
+    barrier, as the whole-job figure sum(bytes) / max over ranks of the copy time (best
+    of ``reps``).  At N=1 the two are the same measurement twice.
+    """
     import torch
     src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     src.fill_(1)
@@ -205,16 +231,30 @@ def h2d_peak_gbs(device, nbytes=512 << 20, reps=10):
     for _ in range(3):
         dst.copy_(src, non_blocking=True)
     torch.cuda.synchronize()
-    best = 0.0
-    for _ in range(reps):
+
+    def timed_copy():
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         dst.copy_(src, non_blocking=True)
         b.record()
         b.synchronize()
-        best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+        return a.elapsed_time(b)
+
+    alone = 0.0
+    for r in range(dist.world):
+        dist.barrier()
+        if r == dist.rank:
+            alone = max(nbytes / (timed_copy() * 1e-3) / 1e9 for _ in range(reps))
+        torch.cuda.synchronize()
+    dist.barrier()
+    best = 0.0
+    for _ in range(reps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = dist.max(timed_copy(), device)
+        best = max(best, dist.world * nbytes / (ms * 1e-3) / 1e9)
     del src, dst
-    return best
+    return alone, best
 
 
 class Layer:
@@ -236,6 +276,7 @@ class Layer:
                                   dtype=self.host[n].dtype, device=device)
                       for n in self.names]
         self.bytes_per_expert = sum(self.sizes)
+        self.sync = torch.zeros((8,), dtype=torch.int32, device=device)
         import numpy as np
         rng = np.random.default_rng(seed + 1000)
         self.hot = sorted(rng.choice(self.E, size=S, replace=False).tolist())
@@ -265,6 +306,7 @@ class Layer:
             trip += trip[-3:]
         self._gather_args = trip + [P(st["miss"].data_ptr()), P(st["n_miss"].data_ptr()),
                                     chunks, lanes]
+        self._step_tail = trip + [chunks, lanes, P(self.sync.data_ptr()), 0]
 
     def reset(self):
         torch = self.torch
@@ -280,6 +322,7 @@ class Layer:
         st["step"].zero_()
         st["miss"].zero_()
         st["n_miss"].zero_()
+        self.sync.zero_()
 
     def snapshot(self):
         return {k: v.cpu().clone() for k, v in self.state.items()
@@ -297,6 +340,19 @@ class Layer:
         rc = self.h.expert_cache_gather(*self._gather_args, stream)
         if rc:
             raise RuntimeError(f"expert_cache_gather rc={rc}")
+
+    def step(self, ids, out, stream):
+        """The whole step in one launch (expert_cache_step)."""
+        mk = ids.numel()
+        rc = self.h.expert_cache_step(
+            ctypes.c_void_p(ids.data_ptr()), mk, self.E, self.S, min(self.E, mk), self.S,
+            *self._sp, self.policy, self.decay, ctypes.c_void_p(out.data_ptr()), 4,
+            *self._step_tail, stream)
+        if rc:
+            raise RuntimeError(f"expert_cache_step rc={rc}")
+
+    def timeouts(self) -> int:
+        return int(self.sync[3].item())
 
 
 def plan_trace(layer: Layer, steps, misses, tokens, seed):
@@ -336,20 +392,19 @@ def check_replay(layer: Layer, final, what):
 
 
 def value_pass(layer, trace_dev, out_dev, W, K, dist):
+    """Device time of K timed steps, one expert_cache_step launch each."""
     import torch
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     layer.reset()
     for t in range(W):
-        layer.manage(trace_dev[t], out_dev[t], stream)
-        layer.gather(stream)
+        layer.step(trace_dev[t], out_dev[t], stream)
     torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for t in range(W, W + K):
-        layer.manage(trace_dev[t], out_dev[t], stream)
-        layer.gather(stream)
+        layer.step(trace_dev[t], out_dev[t], stream)
     b.record()
     torch.cuda.synchronize()
     dist.barrier()
@@ -358,9 +413,20 @@ def value_pass(layer, trace_dev, out_dev, W, K, dist):
 
 
 def kernel_pass(layer, trace_dev, out_dev, W, K):
-    """Per-launch device time of each kernel (events around every launch)."""
+    """Per-launch device time (events around every launch, on the launching stream): the
+    step kernel, then the two-launch form of the same steps from the same state."""
     import torch
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    layer.reset()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)]
+    for t in range(W):
+        layer.step(trace_dev[t], out_dev[t], stream)
+    for i, t in enumerate(range(W, W + K)):
+        evs[i][0].record()
+        layer.step(trace_dev[t], out_dev[t], stream)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    step_us = statistics.mean(e[0].elapsed_time(e[1]) * 1e3 for e in evs)
     layer.reset()
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     for t in range(W):
@@ -384,11 +450,12 @@ def kernel_pass(layer, trace_dev, out_dev, W, K):
         floor.append((x, y))
     torch.cuda.synchronize()
     fl = [x.elapsed_time(y) * 1e3 for x, y in floor]
-    return statistics.mean(man), statistics.mean(gat), statistics.median(fl)
+    return step_us, statistics.mean(man), statistics.mean(gat), statistics.median(fl)
 
 
-def e2e_pass(layer, trace, W, K, tokens):
-    """Through the public per-layer API (ExpertSlotCache.refresh) with host buffers."""
+def e2e_pass(layer, trace, W, K, tokens, dist):
+    """Through the public per-layer API (ExpertSlotCache.refresh) with host buffers; all
+    ranks start the timed loop together."""
     import torch
     import synthetic
     from vllm_expert_cache.cache import ExpertSlotCache
@@ -416,6 +483,8 @@ def e2e_pass(layer, trace, W, K, tokens):
         ids = h_ids[t].to(layer.device, non_blocking=True).view(tokens, TOP_K)
         h_out[t].copy_(cache.refresh(ids).view(-1), non_blocking=True)
     torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for t in range(W, W + K):
@@ -423,12 +492,37 @@ def e2e_pass(layer, trace, W, K, tokens):
         h_out[t].copy_(cache.refresh(ids).view(-1), non_blocking=True)
     b.record()
     torch.cuda.synchronize()
+    dist.barrier()
     ms = a.elapsed_time(b)
+    if cache.step_timeouts():
+        raise RuntimeError("e2e pass: a step kernel wait ran out")
     return ms, h_out, mk * 4, mk * 4, cache
 
 
-def cpu_baseline_port(layer, trace, steps):
-    """The CPU oracle on one host core: C policy step + memcpy of the installed slabs."""
+def plan_trace_oracle(E, S, hot, steps, misses, tokens, seed, policy_code, decay):
+    """Forced-miss routing planned with the C oracle from the warm state: each step has
+    ``misses`` experts absent from the oracle's table and ``8*tokens - misses`` present."""
+    import numpy as np
+    from oracle import policy, policy_c
+    D = TOP_K * tokens
+    st = policy.CacheState.warm(E, S, hot)
+    trace = np.empty((steps, D), dtype=np.int32)
+    rng = np.random.default_rng(seed + 7)
+    for t in range(steps):
+        absent, resident = np.flatnonzero(st.table < 0), np.flatnonzero(st.table >= 0)
+        ch = np.concatenate([rng.choice(absent, misses, replace=False),
+                             rng.choice(resident, D - misses, replace=False)])
+        rng.shuffle(ch)
+        trace[t] = np.concatenate([ch[(r * TOP_K + np.arange(TOP_K)) % D]
+                                   for r in range(tokens)])
+        policy_c.manage(st, trace[t], min(E, D), S, policy_code, decay)
+    return trace
+
+
+def cpu_baseline_port(layer, misses, tokens, seed, seconds):
+    """The CPU oracle on one host core: C policy step + memcpy of the installed slabs,
+    over an oracle-planned forced-miss trace of the same workload, for at least
+    ``seconds`` (steps are added until the time is reached)."""
     import numpy as np
     from oracle import policy, policy_c
     st = policy.CacheState.warm(layer.E, layer.S, layer.hot)
@@ -436,15 +530,18 @@ def cpu_baseline_port(layer, trace, steps):
     dsts = [np.empty(layer.S * b, dtype=np.uint8) for b in layer.sizes]
     for d in dsts:
         d.fill(0)
-    moved = 0
+    trace = plan_trace_oracle(layer.E, layer.S, layer.hot, 4096, misses, tokens, seed,
+                              layer.policy, layer.decay)
+    moved = steps = 0
     t0 = time.perf_counter()
-    for t in range(steps):
-        policy_c.manage(st, trace[t], min(layer.E, trace.shape[1]), layer.S, layer.policy,
-                        layer.decay)
+    while steps < len(trace) and (steps < 8 or time.perf_counter() - t0 < seconds):
+        policy_c.manage(st, trace[steps], min(layer.E, trace.shape[1]), layer.S,
+                        layer.policy, layer.decay)
         policy_c.gather(dsts, hosts, layer.sizes, st.miss, st.n_miss)
         moved += int(st.n_miss[0]) * layer.bytes_per_expert
+        steps += 1
     dt = time.perf_counter() - t0
-    return moved / dt / 1e9, dt
+    return moved / dt / 1e9, dt, steps
 
 
 def reference_timing_trace(steps=4096, E=512, rows=5, k=10, s=1.1, seed=0):
@@ -551,6 +648,72 @@ def policy_sim(dev, policy_code, decay, seed=0, steps=4096, S=64, E=E_EXPERTS, t
             "misses": misses, "lookups": int(steps * mk)}, trace, final, nm_hist.cpu().numpy()
 
 
+def step_graphs(layer, trace, cold, reps=2):
+    """One CUDA graph of ``len(trace)`` layer-steps replayed from the same start state,
+    three ways: one expert_cache_step node per step, the two-launch form (manage_remap +
+    gather nodes), and as many empty kernel nodes (the graph-node floor).  Returns device
+    us per layer-step for each, the installs, and whether both forms ended in the same
+    state (they must: same rules, same kernels' arithmetic)."""
+    import torch
+    dev = layer.device
+    steps = len(trace)
+    ids = torch.from_numpy(trace).to(dev)
+    out = torch.empty_like(ids)
+
+    def start():
+        layer.reset()
+        if cold:
+            st = layer.state
+            st["table"].fill_(-1)
+            st["map_cold"].copy_(torch.arange(layer.E, dtype=torch.int32, device=dev))
+            st["slot_expert"].fill_(-1)
+        torch.cuda.synchronize()
+
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream())
+    graphs = {}
+    for name in ("step", "two_launch", "empty"):
+        start()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            cs = ctypes.c_void_p(side.cuda_stream)
+            for t in range(steps):
+                if name == "step":
+                    layer.step(ids[t], out[t], cs)
+                elif name == "two_launch":
+                    layer.manage(ids[t], out[t], cs)
+                    layer.gather(cs)
+                else:
+                    torch.cuda._sleep(0)
+        graphs[name] = g
+    res, finals = {}, {}
+    for name, g in graphs.items():
+        best = None
+        for _ in range(reps):
+            start()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            best = ms if best is None else min(best, ms)
+        res[name] = round(best * 1e3 / steps, 3)
+        if name != "empty":
+            finals[name] = layer.snapshot()
+    start()
+    graphs["step"].replay()
+    torch.cuda.synchronize()
+    installs = int(layer.sync[4:6].cpu().view(torch.int64)[0])
+    same = all(torch.equal(finals["step"][k], finals["two_launch"][k]) for k in finals["step"])
+    timeouts = layer.timeouts()
+    del graphs
+    return {"step_us_per_layer_step": res["step"],
+            "two_launch_us_per_layer_step": res["two_launch"],
+            "empty_node_us": res["empty"], "installs": installs, "steps": steps,
+            "same_final_state": same, "step_wait_timeouts": timeouts}
+
+
 def policy_sim_cpu_baseline(trace, policy_code, decay, final, nm_gpu, S=64, E=E_EXPERTS,
                             max_distinct=None, max_inserts=None):
     """The same trace through the C oracle on one core: its time per step, and the check
@@ -589,7 +752,8 @@ def run_ours(a, dist):
     if a.sweep:
         points = [(S, m, T) for T in (1, 4) for S in (16, 32, 64, 96) for m in (1, 2, 4, 8)
                   if TOP_K * T <= S]
-    peak = h2d_peak_gbs(dev)
+    peak_alone, peak_all = h2d_peaks(dev, dist)
+    peak = peak_all / dist.world          # this rank's share of the concurrent host link
     layer = None
     for S, m, T in points:
         if layer is None or layer.S != S:
@@ -605,9 +769,12 @@ def run_ours(a, dist):
         bytes_step = m * layer.bytes_per_expert
         total_bytes = dist.sum(float(K * bytes_step), dev)
         value = total_bytes / (ms_max * 1e-3) / 1e9
-        man_us, gat_us, floor_us = kernel_pass(layer, trace_dev, out_dev, W, K)
+        if layer.timeouts():
+            raise RuntimeError("value pass: a step kernel wait ran out")
+        step_us, man_us, gat_us, floor_us = kernel_pass(layer, trace_dev, out_dev, W, K)
         check_replay(layer, final, "kernel pass")
-        achieved = bytes_step / (gat_us * 1e-6) / 1e9
+        achieved = bytes_step / (step_us * 1e-6) / 1e9
+        alone_min = dist.min(peak_alone, dev)
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": dist.world, "steps": K, "warmup": W,
@@ -626,21 +793,36 @@ def run_ours(a, dist):
                       f"MiB host experts, {S * layer.bytes_per_expert >> 20} MiB slots "
                       f"(L2 {L2_BYTES >> 20} MiB)",
                 "parallelism": f"replicas x{dist.world} (no collective on the cache path)"},
+            "host_link": {
+                "alone_gbs_per_rank_min": round(alone_min, 3),
+                "concurrent_gbs_all_ranks": round(peak_all, 3),
+                "concurrent_gbs_per_rank": round(peak, 3),
+                "gather_frac_of_concurrent": round(value / peak_all, 4),
+                "how": "pinned 512 MiB cudaMemcpyAsync H2D per rank, best of 8; alone = "
+                       "ranks take turns, concurrent = all ranks after a barrier, "
+                       "sum(bytes) / max time"},
             "host_link_peak_gbs": round(peak, 3),
-            "host_link_frac": round(value / dist.world / peak, 4),
+            "host_link_frac": round(value / peak_all, 4),
+            "step_us_per_launch": round(step_us, 3),
+            "two_launch": {"manage_us_per_launch": round(man_us, 3),
+                           "gather_us_per_launch": round(gat_us, 3),
+                           "gbs": round(bytes_step / ((man_us + gat_us) * 1e-6) / 1e9, 3)},
             "manage_us_per_layer": round(man_us, 3),
-            "gather_us_per_launch": round(gat_us, 3),
             "empty_kernel_us": round(floor_us, 3),
             "roofline": {"bound": "host-link", "achieved": round(achieved, 3),
                          "peak": round(peak, 3), "unit": "GB/s",
                          "frac": round(achieved / peak, 4),
-                         "traffic": GATHER_DRAM_BYTES if (S, m, T) == (64, 4, 1) else None,
-                         "peak_source": "pinned cudaMemcpyAsync H2D, measured in this run"},
-            "gpu_launches": 2 * K,
+                         "traffic": STEP_DRAM_BYTES if (S, m, T) == (64, 4, 1) else None,
+                         "traffic_source": STEP_DRAM_SOURCE,
+                         "kernel": "step_kernel (expert_cache_step)",
+                         "peak_source": "pinned cudaMemcpyAsync H2D, measured in this run "
+                                        "with every rank copying at once"},
+            "gpu_launches": K,
+            "host_cores": len(os.sched_getaffinity(0)),
             "clocks": clk.summary(),
         }
         if not a.sweep and not a.no_e2e:
-            ms_e, h_out, hb, db, _ = e2e_pass(layer, trace, W, K, T)
+            ms_e, h_out, hb, db, _ = e2e_pass(layer, trace, W, K, T, dist)
             if not torch.equal(h_out[W:], out_dev[W:].cpu()):
                 raise RuntimeError("e2e pass: slot ids differ from the C-ABI pass")
             ms_e = dist.max(ms_e, dev)
@@ -668,18 +850,112 @@ def run_ours(a, dist):
             res["workload"] = ("E512 S257, 5 rows x top-10 Zipf(1.1) repeated (steady "
                                "state, all hits after the first call), LFU")
             line["manage_reference_shape"] = res
+            if S == 64 and T == 1:
+                # whole layer-steps (policy + remap + gather) as vLLM's decode graph replays
+                # them: a no-miss step (8 resident experts routed every step) and config 1
+                # (sticky Zipf from a cold cache, with its installs gathered)
+                hit = np.tile(np.array(layer.hot[:TOP_K], dtype=np.int32), (4096, 1))
+                no_miss = step_graphs(layer, hit, cold=False)
+                no_miss["workload"] = ("4096 steps routing the same 8 resident experts "
+                                       "(no installs), E128 S64, Qwen3-30B-A3B slabs")
+                from synthetic import sticky_zipf_trace
+                cfg1 = step_graphs(layer, sticky_zipf_trace(0, steps=4096), cold=True, reps=1)
+                cfg1["workload"] = ("config 1 trace (sticky Zipf, seed 0) from a cold cache, "
+                                    "E128 S64 LFU, installs gathered (Qwen3-30B-A3B slabs)")
+                line["step_graph"] = {"no_miss": no_miss, "config1": cfg1}
+                layer.reset()
         if not a.sweep and not a.no_cpu and dist.rank == 0 and dist.world == 1:
-            n = min(K, 200)
-            gbs, dt = cpu_baseline_port(layer, trace[W:], n)
+            gbs, dt, n = cpu_baseline_port(layer, m, T, a.seed, a.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
-                "sample": f"{n} steps of the same trace: C restatement of the policy step "
-                          f"+ memcpy of the installed slabs host->host ({dt:.2f} s)"}
+                "host_cores": len(os.sched_getaffinity(0)),
+                "sample": f"{n} steps of the same workload ({m} forced misses per step, "
+                          f"oracle-planned): C restatement of the policy step + memcpy of "
+                          f"the installed slabs host->host, one core, {dt:.2f} s"}
+        if not a.sweep and not a.no_decode and dist.world == 1:
+            del trace_dev, out_dev
+            layer = None
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
+            try:
+                line["decode"] = decode_leg(a)
+            except Exception as e:   # the microbench line still prints
+                line["decode"] = {"error": repr(e)[-800:]}
         if dist.rank == 0:
             print(json.dumps(line), flush=True)
-        del trace_dev, out_dev
     dist.barrier()
     dist.close()
+
+
+# ---------------------------------------------------------------------------------------
+# decode leg: end-to-end decode through vLLM (bench_decode.py), N=1 only
+
+DECODE_WORKLOAD = ("config 3: synthetic Qwen3-30B-A3B W8A8 int8 experts (48 layers, hidden "
+                   "2048, 32q/4kv x 128, 128 experts x moe_intermediate 768, top-8, vocab "
+                   "151936; attention bf16), random-init normal(0, 0.02) weights, TP1, "
+                   "batch 1, 128-token seeded random prompt, greedy, {gen} generated tokens, "
+                   "vLLM 0.22 with CUDA graphs; experts offloaded with "
+                   "--cpu-offload-params experts")
+
+
+def _decode_view(r: dict | None) -> dict | None:
+    if r is None:
+        return None
+    cache = r.get("cache") or {}
+    out = {"mode": r["mode"], "decode_tok_s": r["decode_tok_s"],
+           "frac_of_resident": r["frac_of_resident"],
+           "tokens_identical_to_resident": r["tokens_match_resident"],
+           "max_abs_logprob_diff_before_divergence": round(r["max_abs_logprob_diff"], 6),
+           "first_divergent_token": r["first_divergent_token"],
+           "resident_top2_gap_at_divergence": r["resident_top2_gap_at_divergence"],
+           "init_s": r.get("init_s"), "wall_s": r.get("wall_s")}
+    if cache:
+        out.update(installs_per_layer_step=cache.get("installs_per_layer_step"),
+                   layer_steps=cache.get("layer_steps"), installs=cache.get("installs"),
+                   armed_layers=cache.get("armed_layers"),
+                   step_wait_timeouts=cache.get("step_wait_timeouts"))
+    return out
+
+
+def decode_leg(a) -> dict:
+    """Resident, cached (``--decode-slots``) and vLLM's uncached offload, with the model's
+    own routing; resident and cached again with every layer replaying a sticky-Zipf trace
+    (routing churn with the config-1 locality).  One vLLM engine process per mode."""
+    import bench_decode as bd
+    import tempfile
+    args = bd.parser().parse_args([
+        "--slots", str(a.decode_slots), "--gen", str(a.decode_gen),
+        "--routing", "model", "sticky-zipf", "--budget-s", str(a.decode_budget_s),
+        "--mode-timeout", "600", "--logdir",
+        str(Path(tempfile.gettempdir()) / "expert_cache_bench_decode")])
+    modes = [m for m in bd.plan_modes(args) if m["name"] != "offload-churn"]
+    got = bd.run_suite(args, modes, echo=False)
+    by = {r["mode"]: r for r in got["results"]}
+    S = a.decode_slots
+    res, cached, off = by.get("resident"), by.get(f"slots{S}"), by.get("offload")
+    res_c, cached_c = by.get("resident-churn"), by.get(f"slots{S}-churn")
+    out = {"workload": DECODE_WORKLOAD.format(gen=a.decode_gen), "slots": S,
+           "experts": 128, "policy": args.policy,
+           "resident_tok_s": res and res["decode_tok_s"],
+           "cached_tok_s": cached and cached["decode_tok_s"],
+           "frac_of_resident": cached and cached["frac_of_resident"],
+           "offload_uncached_tok_s": off and off["decode_tok_s"],
+           "offload_uncached_frac_of_resident": off and off["frac_of_resident"],
+           "cached": _decode_view(cached), "offload_uncached": _decode_view(off),
+           "churn": {"routing": "every layer replays its own sticky-Zipf trace (config-1 "
+                                "locality: p_keep 0.7, Zipf(1.1)), both modes",
+                     "resident_tok_s": res_c and res_c["decode_tok_s"],
+                     "cached_tok_s": cached_c and cached_c["decode_tok_s"],
+                     "frac_of_resident": cached_c and cached_c["frac_of_resident"],
+                     "cached": _decode_view(cached_c)},
+           "parity": "greedy tokens of each mode against its resident run; logprob "
+                     "difference of the chosen tokens before any divergence",
+           "all_within_1e-2_before_divergence":
+               got["summary"]["all_within_1e-2_before_divergence"],
+           "skipped": got["summary"]["skipped"], "failed": got["summary"]["failed"],
+           "wall_s": got["summary"]["wall_s"]}
+    return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -687,6 +963,7 @@ def run_ours(a, dist):
 
 def _ref_worker(args):
     shm_name, shapes, sizes, S, hot, trace, policy_code, decay, steps, warm = args
+    # `steps` layer-steps after `warm` untimed ones, over the oracle-planned trace
     import numpy as np
     from multiprocessing import shared_memory
     from oracle import policy, policy_c
@@ -721,7 +998,6 @@ def run_reference(a, dist):
     from multiprocessing import shared_memory
 
     import numpy as np
-    from oracle import policy, policy_c
     if dist.rank != 0:
         return
     S, m, T = a.slots, a.misses, a.tokens
@@ -737,20 +1013,11 @@ def run_reference(a, dist):
         buf[:] = rng.integers(0, 256, size=total, dtype=np.uint8)
         del buf
         hot = sorted(np.random.default_rng(a.seed + 1000).choice(E, S, replace=False).tolist())
-        # plan the forced-miss trace with the oracle (untimed)
-        D = TOP_K * T
-        st = policy.CacheState.warm(E, S, hot)
         W, K = a.warmup, a.steps
-        trace = np.empty((W + K, D), dtype=np.int32)
-        prng = np.random.default_rng(a.seed + 7)
-        for t in range(W + K):
-            absent, resident = np.flatnonzero(st.table < 0), np.flatnonzero(st.table >= 0)
-            ch = np.concatenate([prng.choice(absent, m, replace=False),
-                                 prng.choice(resident, D - m, replace=False)])
-            prng.shuffle(ch)
-            trace[t] = np.concatenate([ch[(r * TOP_K + np.arange(TOP_K)) % D]
-                                       for r in range(T)])
-            policy_c.manage(st, trace[t], min(E, D), S, policy_code, a.decay)
+        # A "step" of this arm is R consecutive layer-steps, R chosen so that the timed K
+        # steps take seconds rather than milliseconds on every worker.
+        R = max(1, -(-REF_LAYER_STEPS // K))
+        trace = plan_trace_oracle(E, S, hot, W + K * R, m, T, a.seed, policy_code, a.decay)
         cores = len(os.sched_getaffinity(0))
         try:
             import psutil
@@ -761,7 +1028,7 @@ def run_reference(a, dist):
         workers = max(1, min(cores, int(avail * 0.3 // per_worker)))
         sizes = list(shapes_pe)
         shapes = [E * b for b in shapes_pe]
-        job = (shm.name, shapes, sizes, S, hot, trace, policy_code, a.decay, K, W)
+        job = (shm.name, shapes, sizes, S, hot, trace, policy_code, a.decay, K * R, W)
         ctx = mp.get_context("spawn")
         with ctx.Pool(workers) as pool:
             res = pool.map(_ref_worker, [job] * workers)
@@ -780,10 +1047,12 @@ def run_reference(a, dist):
                        "policy": a.policy, "decay": a.decay,
                        "parallelism": f"{workers} independent CPU replicas"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": workers,
-                             "kind": "port",
-                             "sample": f"{workers} processes x {K} steps: C restatement of "
-                                       "the reference policy step + memcpy of the installed "
-                                       "slabs host->host (the reference has no CPU gather)"},
+                             "kind": "port", "host_cores": cores,
+                             "sample": f"{workers} processes x {K} steps of {R} layer-steps "
+                                       f"({span:.2f} s): C restatement of the reference "
+                                       "policy step + memcpy of the installed slabs "
+                                       "host->host (the reference has no CPU gather)"},
+            "host_cores": cores,
             "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
         }

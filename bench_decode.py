@@ -128,9 +128,17 @@ def _seed(name: str, base: int = 1234) -> int:
     return (base * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFF
 
 
+# Experts drawn per random call while initialising a quantised expert tensor (one fp32
+# chunk of 16 Qwen3-30B-A3B w13 slabs is 200 MB of scratch).
+INIT_CHUNK = 16
+
+
 def init_synthetic_weights(model, std: float = 0.02) -> None:
     """normal(0, std) everywhere; int8 / fp8 weights quantised per output row with their
-    fp32 ``*_scale`` set to absmax/qmax (127 / 448); norm weights 1."""
+    fp32 ``*_scale`` set to absmax/qmax (127 / 448); norm weights 1.  Every tensor draws
+    from its own generator seeded by its name, on the tensor's device, in fixed chunks of
+    experts, so resident and offloaded runs (UVA views of host memory are CUDA tensors)
+    initialise identical weights."""
     import torch
     params = dict(model.named_parameters())
     quantised = {torch.int8: 127.0, torch.float8_e4m3fn: 448.0}
@@ -145,15 +153,16 @@ def init_synthetic_weights(model, std: float = 0.02) -> None:
                 lead = p.shape[0] if p.dim() == 3 else 1
                 qv = p.view(lead, *p.shape[-2:])
                 sv = scale.view(lead, p.shape[-2], -1)
-                for e in range(lead):       # one expert (or one matrix) at a time
-                    w = torch.randn(qv.shape[1:], generator=g, device=p.device,
-                                    dtype=torch.float32) * std
+                for e0 in range(0, lead, INIT_CHUNK):   # a chunk of experts at a time
+                    e1 = min(lead, e0 + INIT_CHUNK)
+                    w = torch.randn((e1 - e0,) + tuple(qv.shape[1:]), generator=g,
+                                    device=p.device, dtype=torch.float32) * std
                     s = w.abs().amax(dim=-1, keepdim=True).clamp_min(1e-8) / qmax
                     q = (w / s).clamp_(-qmax, qmax)
                     if p.dtype == torch.int8:
                         q = torch.round(q)
-                    qv[e].copy_(q.to(p.dtype))
-                    sv[e].copy_(s.to(sv.dtype).expand_as(sv[e]))
+                    qv[e0:e1].copy_(q.to(p.dtype))
+                    sv[e0:e1].copy_(s.to(sv.dtype).expand_as(sv[e0:e1]))
             elif name.endswith("_scale") and name[:-6] in params \
                     and params[name[:-6]].dtype in quantised:
                 continue                     # written with its weight
@@ -183,14 +192,89 @@ def cache_stats_on_worker(worker) -> list:
     return out
 
 
+# Benchmark-only routing override: with BENCH_DECODE_ROUTING=sticky-zipf every MoE layer's
+# routing ids replay that layer's own sticky-Zipf trace (the config-1 locality model: each
+# of the 8 positions keeps the previous token's expert with p=0.7, else draws Zipf(1.1)
+# over a seeded permutation), one trace row per token, seeds 1000 + layer index.  The
+# router's top-k weights are kept.  A device counter per layer picks the row, so the
+# override runs inside vLLM's CUDA graphs (3 small torch kernels per layer per decode
+# step, paid by every mode that uses the override, resident included).
+ROUTING_ENV = "BENCH_DECODE_ROUTING"
+TRACE_ROWS = 4096
+
+
+class _TraceRouting:
+    def __init__(self, router, seed: int):
+        self.router, self.seed = router, seed
+        self.orig = router.select_experts
+        self.tr = self.ctr = self.ar = None
+
+    def _init(self, ids):
+        import torch
+        from synthetic import sticky_zipf_trace
+        k = ids.size(1)
+        E = int(self.router.global_num_experts)
+        tr = sticky_zipf_trace(self.seed, steps=TRACE_ROWS, E=E, k=k)
+        self.tr = torch.from_numpy(tr).to(device=ids.device, dtype=ids.dtype)
+        self.ctr = torch.zeros(1, dtype=torch.int64, device=ids.device)
+
+    def reset(self):
+        if self.ctr is not None:
+            self.ctr.zero_()
+
+    def __call__(self, hidden_states, router_logits, *, input_ids=None):
+        import torch
+        w, ids = self.orig(hidden_states, router_logits, input_ids=input_ids)
+        if ids.dim() != 2:
+            return w, ids
+        if self.tr is None:
+            self._init(ids)
+        n = ids.size(0)
+        if n == 1:
+            idx = self.ctr
+        else:
+            if self.ar is None or self.ar.numel() < n:
+                self.ar = torch.arange(max(n, 8192), dtype=torch.int64, device=ids.device)
+            idx = (self.ctr + self.ar[:n]).remainder_(TRACE_ROWS)
+        new = self.tr.index_select(0, idx)
+        self.ctr.add_(n).remainder_(TRACE_ROWS)     # always a valid row index
+        return w, new
+
+
+def install_trace_routing(model) -> int:
+    """Wrap every FusedMoE layer's router (in model order) with its trace replay."""
+    from vllm.model_executor.layers.fused_moe.layer import FusedMoE
+    n = 0
+    for m in model.modules():
+        if isinstance(m, FusedMoE) and getattr(m, "router", None) is not None:
+            m.router.select_experts = _TraceRouting(m.router, 1000 + n)
+            n += 1
+    return n
+
+
+def reset_routing_on_worker(worker) -> int:
+    """collective_rpc target: restart every layer's trace at row 0."""
+    model = worker.model_runner.get_model()
+    n = 0
+    for m in model.modules():
+        r = getattr(getattr(m, "router", None), "select_experts", None)
+        if isinstance(r, _TraceRouting):
+            r.reset()
+            n += 1
+    return n
+
+
 def register_synthetic_loader() -> None:
     """vllm.general_plugins entry point of the benchmark (not of the product)."""
+    import os
     from vllm.model_executor.model_loader import register_model_loader
     from vllm.model_executor.model_loader.dummy_loader import DummyModelLoader
 
     class SyntheticW8A8Loader(DummyModelLoader):
         def load_weights(self, model, model_config) -> None:
             init_synthetic_weights(model)
+            if os.environ.get(ROUTING_ENV) == "sticky-zipf":
+                install_trace_routing(model)
 
     register_model_loader(LOAD_FORMAT)(SyntheticW8A8Loader)
 
@@ -243,7 +327,12 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
     env["EXPERT_CACHE_POLICY"] = args.policy
     env["EXPERT_CACHE_STATS"] = "1" if args.stats else "0"
     env.pop("EXPERT_CACHE_SPLIT_WIDE", None)
-    env["EXPERT_CACHE_PREFETCH"] = "1" if mode.get("prefetch") else "0"
+    env["EXPERT_CACHE_PREFETCH"] = str(mode.get("prefetch") or 0)
+    if mode.get("policy"):
+        env["EXPERT_CACHE_POLICY"] = mode["policy"]
+    env.pop(ROUTING_ENV, None)
+    if mode.get("routing"):
+        env[ROUTING_ENV] = mode["routing"]
     if mode.get("split"):
         env["EXPERT_CACHE_SPLIT_WIDE"] = str(mode["split"])
     if args.deterministic:
@@ -305,11 +394,19 @@ def child(mode: dict, a) -> None:
     # random-init model's greedy output repeats one token, which makes routing repeat)
     timed = greedy if a.temperature == 0 else dict(
         temperature=a.temperature, seed=a.seed, ignore_eos=True, detokenize=False)
-    llm.generate(prompts, SamplingParams(max_tokens=32, **timed), use_tqdm=False)  # warm
+
+    def generate(p, sp):
+        # with the trace routing, every generate starts each layer's trace at row 0, so all
+        # modes see the same routing sequence
+        if mode.get("routing"):
+            llm.collective_rpc(reset_routing_on_worker)
+        return llm.generate(p, sp, use_tqdm=False)
+
+    generate(prompts, SamplingParams(max_tokens=32, **timed))  # warm
     # parity run: the first prompt alone, or (--parity-batch) the whole batch so that its
     # decode steps have the timed runs' width; sequences are concatenated in prompt order
-    refs = llm.generate(prompts if a.parity_batch else prompts[:1],
-                        SamplingParams(max_tokens=a.gen, logprobs=2, **greedy), use_tqdm=False)
+    refs = generate(prompts if a.parity_batch else prompts[:1],
+                    SamplingParams(max_tokens=a.gen, logprobs=2, **greedy))
     tokens, lps, gaps = [], [], []
     for r in refs:
         ref = r.outputs[0]
@@ -323,6 +420,8 @@ def child(mode: dict, a) -> None:
     for n in (1, a.gen):
         best = None
         for _ in range(2):
+            if mode.get("routing"):
+                llm.collective_rpc(reset_routing_on_worker)
             t = time.perf_counter()
             llm.generate(prompts, SamplingParams(max_tokens=n, **timed), use_tqdm=False)
             dt = time.perf_counter() - t
@@ -339,7 +438,8 @@ def child(mode: dict, a) -> None:
             installs = sum(x.get("installs", 0) for x in layers)
             cache = {"armed_layers": len(layers), "layer_steps": steps,
                      "mirrored": layers[0]["mirrored"], "bound": layers[0]["bound"],
-                     "method": layers[0]["method"]}
+                     "method": layers[0]["method"],
+                     "step_wait_timeouts": sum(x.get("step_timeouts", 0) for x in layers)}
             cache["prefetch_linked"] = sum(bool(x.get("prefetch_linked")) for x in layers)
             if "installs" in layers[0]:
                 cache.update(installs=installs,
@@ -350,7 +450,8 @@ def child(mode: dict, a) -> None:
                 cache.update(prefetch_installs=pf,
                              prefetch_installs_per_layer_step=round(pf / max(steps, 1), 4))
     out = {"mode": mode["name"], "slots": mode.get("slots"), "split_wide": mode.get("split", 0),
-           "prefetch": bool(mode.get("prefetch")),
+           "prefetch": mode.get("prefetch") or 0, "routing": mode.get("routing") or "model",
+           "policy": mode.get("policy") or a.policy,
            "offload": bool(mode.get("offload")),
            "tp": a.tp, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
            "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
@@ -358,7 +459,7 @@ def child(mode: dict, a) -> None:
     print(json.dumps({"decode_result": out}), flush=True)
 
 
-def main(argv=None):
+def parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser()
     ap.add_argument("--arch", choices=sorted(MODELS), default="qwen3-30b-a3b")
     ap.add_argument("--layers", type=int, default=0, help="0 = the architecture's own")
@@ -371,6 +472,9 @@ def main(argv=None):
     ap.add_argument("--gen", type=int, default=512)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--policy", default="lfu")
+    ap.add_argument("--policies", nargs="*", default=[],
+                    help="EXPERT_CACHE_POLICY values: every slot count runs once per value "
+                         "(default: --policy alone)")
     ap.add_argument("--quant", choices=["int8", "int8-experts", "fp8", "bf16"],
                     default="int8-experts")
     ap.add_argument("--offload-gb", type=float, default=64.0)
@@ -378,8 +482,9 @@ def main(argv=None):
     ap.add_argument("--no-resident", action="store_true",
                     help="skip the resident mode: the first mode run is the comparison base")
     ap.add_argument("--stats", action="store_true",
-                    help="EXPERT_CACHE_STATS=1: count installs (adds one small kernel per "
-                         "layer-step, so keep it off for timing)")
+                    help="EXPERT_CACHE_STATS=1: also count installs of the two-launch path "
+                         "and of prefetches (one small kernel per layer-step each); the "
+                         "single-launch step counts its own installs either way")
     ap.add_argument("--moe-backend", default="auto",
                     help="vLLM MoE backend; the cache needs a modular (non-monolithic) one, "
                          "e.g. 'triton' where vLLM's default would be flashinfer_trtllm")
@@ -392,6 +497,12 @@ def main(argv=None):
     ap.add_argument("--temperature", type=float, default=0.0,
                     help="timed runs only: 0 = greedy; > 0 = seeded sampling (the parity "
                          "run stays greedy)")
+    ap.add_argument("--routing", nargs="*", default=["model"],
+                    choices=["model", "sticky-zipf"],
+                    help="'model': the random-init router's own choice; 'sticky-zipf': every "
+                         "layer replays its own config-1 trace (benchmark-only override). "
+                         "Each kind runs its own resident / offload / slots modes and is "
+                         "compared with its own resident run")
     ap.add_argument("--debug-calls", type=int, default=0,
                     help="EXPERT_CACHE_DEBUG: log the first N MoE calls per armed layer")
     ap.add_argument("--control", action="store_true",
@@ -400,73 +511,121 @@ def main(argv=None):
                     help="EXPERT_CACHE_SPLIT_WIDE values: every slot count runs once per "
                          "value (0 = the reference's read-through of wide steps)")
     ap.add_argument("--prefetch", type=int, nargs="*", default=[],
-                    help="EXPERT_CACHE_PREFETCH values (0/1): every slot count runs once "
-                         "per value")
+                    help="EXPERT_CACHE_PREFETCH values (predictions per token, 0 = off): "
+                         "every slot count runs once per value")
     ap.add_argument("--parity-batch", action="store_true",
                     help="greedy parity run over the whole batch instead of its first prompt")
     ap.add_argument("--mode-timeout", type=int, default=1200)
+    ap.add_argument("--budget-s", type=float, default=0,
+                    help="stop starting new modes once this much wall time has passed "
+                         "(0 = no limit); skipped modes are listed in the summary")
     ap.add_argument("--logdir", default=str(Path(tempfile.gettempdir()) / "expert_cache_decode"),
                     help="per-mode engine logs")
     ap.add_argument("--child", default=None)
     ap.add_argument("--model", default=None)
-    a = ap.parse_args(argv)
-    if a.child:
-        return child(json.loads(a.child), a)
+    return ap
 
+
+def plan_modes(a) -> list[dict]:
+    """Every mode of the run, grouped by routing kind; the first mode of a kind that keeps
+    the experts resident is that kind's comparison base."""
+    modes = []
+    for routing in a.routing:
+        tag = "" if routing == "model" else "-churn"
+        extra = {} if routing == "model" else {"routing": routing}
+        if not a.no_resident:
+            modes.append({"name": "resident" + tag, **extra})
+        if a.control:
+            modes.append({"name": "resident-again" + tag, **extra})
+        if not a.no_offload_baseline:
+            modes.append({"name": "offload" + tag, "offload": True,
+                          "offload_gb": a.offload_gb, **extra})
+        for pol in (a.policies or [None]):
+            for sl in a.slots:
+                for v in (a.split_wide or [0]):
+                    for f in (a.prefetch or [0]):
+                        name = (f"slots{sl}" + (f"-{pol}" if pol else "") +
+                                (f"-split{v}" if v else "") + (f"-prefetch{f}" if f else "") +
+                                tag)
+                        modes.append({"name": name, "slots": sl, "split": v, "prefetch": f,
+                                      "policy": pol, "offload": True,
+                                      "offload_gb": a.offload_gb, **extra})
+    return modes
+
+
+def compare(r: dict, base: dict) -> dict:
+    """Speed and greedy parity of one mode against its base (resident) run."""
+    r["base_mode"] = base["mode"]
+    r["frac_of_resident"] = round(r["decode_tok_s"] / base["decode_tok_s"], 4)
+    r["tokens_match_resident"] = r["tokens"] == base["tokens"]
+    first = next((i for i, (x, y) in enumerate(zip(r["tokens"], base["tokens"])) if x != y),
+                 None)
+    r["first_divergent_token"] = first
+    # logprobs of the same chosen tokens: every position before the first divergence
+    upto = len(r["tokens"]) if first is None else first
+    r["max_abs_logprob_diff"] = max(
+        (abs(x - y) for x, y in zip(r["logprobs"][:upto], base["logprobs"][:upto])),
+        default=0.0)
+    # at a divergence: how close the resident run's own top-2 were (a near-tie flip)
+    r["resident_top2_gap_at_divergence"] = (None if first is None
+                                            else round(base["gaps"][first], 5))
+    return r
+
+
+def run_suite(a, modes=None, echo=True) -> dict:
+    """Run every mode (one vLLM engine process each) and compare each with its base."""
     logdir = Path(a.logdir)
     logdir.mkdir(parents=True, exist_ok=True)
     tmp = Path(tempfile.mkdtemp(prefix="expert_cache_decode_"))
     model_dir, site = tmp / "model", tmp / "site"
     write_model_dir(model_dir, a.layers, a.prompt + a.gen + 16, a.quant, a.arch)
     write_plugin_site(site)
-    modes = [] if a.no_resident else [{"name": "resident"}]
-    if a.control:
-        modes.append({"name": "resident-again"})   # the engine's own run-to-run spread
-    if not a.no_offload_baseline:
-        modes.append({"name": "offload", "offload": True, "offload_gb": a.offload_gb})
-    modes += [{"name": f"slots{s}" + (f"-split{v}" if v else "") + ("-prefetch" if f else ""),
-               "slots": s, "split": v, "prefetch": f, "offload": True,
-               "offload_gb": a.offload_gb}
-              for s in a.slots for v in (a.split_wide or [0]) for f in (a.prefetch or [0])]
-    results = []
-    base = None
+    modes = plan_modes(a) if modes is None else modes
+    t0 = time.time()
+    results, skipped, failed = [], [], {}
+    bases: dict[str, dict] = {}
     for m in modes:
-        r = run_mode(m, a, model_dir, site, logdir)
-        if base is None:
-            base = r
-        r["frac_of_resident"] = round(r["decode_tok_s"] / base["decode_tok_s"], 4)
-        r["tokens_match_resident"] = r["tokens"] == base["tokens"]
-        first = next((i for i, (x, y) in enumerate(zip(r["tokens"], base["tokens"]))
-                      if x != y), None)
-        r["first_divergent_token"] = first
-        # logprobs of the same chosen tokens: every position before the first divergence
-        upto = len(r["tokens"]) if first is None else first
-        r["max_abs_logprob_diff"] = max(
-            (abs(x - y) for x, y in zip(r["logprobs"][:upto], base["logprobs"][:upto])),
-            default=0.0)
-        # at a divergence: how close the resident run's own top-2 were (a near-tie flip)
-        r["resident_top2_gap_at_divergence"] = (None if first is None
-                                                else round(base["gaps"][first], 5))
+        if a.budget_s and time.time() - t0 > a.budget_s:
+            skipped.append(m["name"])
+            continue
+        try:
+            r = run_mode(m, a, model_dir, site, logdir)
+        except Exception as e:        # report and go on: one mode must not sink the rest
+            failed[m["name"]] = repr(e)[-600:]
+            continue
+        kind = m.get("routing") or "model"
+        if kind not in bases and not m.get("offload"):
+            bases[kind] = r
+        base = bases.get(kind, r)
+        compare(r, base)
         slim = {k: v for k, v in r.items() if k not in ("logprobs", "gaps")}
         slim["tokens"] = r["tokens"][:16]
         slim.update(moe_backend=a.moe_backend, deterministic=a.deterministic,
                     temperature=a.temperature,
                     arch=a.arch, layers=a.layers or MODELS[a.arch][0]["num_hidden_layers"],
-                    prompt=a.prompt, gen=a.gen, policy=a.policy, quant=a.quant,
-                    parity_batch=a.parity_batch)
-        print(json.dumps(slim), flush=True)
+                    prompt=a.prompt, gen=a.gen, quant=a.quant, parity_batch=a.parity_batch)
+        if echo:
+            print(json.dumps(slim), flush=True)
         results.append(slim)
     # the chosen tokens' logprobs within 1e-2 of the resident run's at every position the
     # two runs share (before any divergence); divergences are reported with the resident
     # run's own top-1/top-2 margin at that position
-    ok = all(r["max_abs_logprob_diff"] <= 1e-2 for r in results)
-    print(json.dumps({"summary": "decode", "all_within_1e-2_before_divergence": ok,
-                      "tokens_identical": {r["mode"]: r["tokens_match_resident"]
-                                           for r in results},
-                      "decode_tok_s": {r["mode"]: r["decode_tok_s"] for r in results},
-                      "frac_of_resident": {r["mode"]: r["frac_of_resident"] for r in results}}),
-          flush=True)
-    return 0 if ok else 1
+    ok = all(r["max_abs_logprob_diff"] <= 1e-2 for r in results) and not failed
+    summary = {"summary": "decode", "all_within_1e-2_before_divergence": ok,
+               "tokens_identical": {r["mode"]: r["tokens_match_resident"] for r in results},
+               "decode_tok_s": {r["mode"]: r["decode_tok_s"] for r in results},
+               "frac_of_resident": {r["mode"]: r["frac_of_resident"] for r in results},
+               "skipped": skipped, "failed": failed, "wall_s": round(time.time() - t0, 1)}
+    if echo:
+        print(json.dumps(summary), flush=True)
+    return {"results": results, "summary": summary, "ok": ok}
+
+
+def main(argv=None):
+    a = parser().parse_args(argv)
+    if a.child:
+        return child(json.loads(a.child), a)
+    return 0 if run_suite(a)["ok"] else 1
 
 
 if __name__ == "__main__":

@@ -254,6 +254,46 @@ EXPERT_CACHE_API int expert_cache_gather(void* d0, const void* s0, long b0, void
                         void* d5, const void* s5, long b5, const int* miss,
                         const int* n_miss, int chunks, int lanes, cudaStream_t stream);
 
+/* Largest slot count of expert_cache_step: its policy step runs in one CTA of 256 threads,
+ * one slot per thread. */
+#define EXPERT_CACHE_STEP_MAX_SLOTS 256
+/* Wait bound of expert_cache_step when max_wait_us is 0: one second. */
+#define EXPERT_CACHE_STEP_DEFAULT_WAIT_US 1000000
+
+/* One whole cached step in a single launch: expert_cache_manage_remap followed by
+ * expert_cache_gather of the six triples, with the same arguments, meaning and results.
+ *
+ * A decode step that installs nothing is then one kernel node instead of two.  Inside the
+ * launch, the first CTA to start runs the policy step and the remap; the other CTAs wait
+ * for it (a device flag, bounded by max_wait_us, 0 = EXPERT_CACHE_STEP_DEFAULT_WAIT_US) and
+ * then every CTA copies its share of the miss list's slabs.
+ *
+ *   sync   [8] int32 (8-byte aligned), zero before the first call and then owned by these
+ *          calls.  sync[0..2] are the launch's arrival / departure counters and ready
+ *          flag, which the last CTA to leave clears again.  sync[3] is a running count of
+ *          CTAs whose wait ran out: such a CTA copies nothing, so a non-zero sync[3] means
+ *          some installed slot may not hold its expert's bytes.  sync[4..5] hold a
+ *          running int64 count of installed experts (the sum of n_miss over calls).
+ *          sync[6..7] are reserved.  Use one sync array per cache (per layer); launches
+ *          sharing one must be ordered on one stream.
+ *
+ * Returns -1 on the rules of expert_cache_manage_remap and expert_cache_gather, when
+ * S > EXPERT_CACHE_STEP_MAX_SLOTS, when sync is NULL or not 8-byte aligned, or when
+ * max_wait_us < 0.
+ *
+ * Replaces: the two launches of the reference's per-layer step (cache.py:118-161:
+ * expert_cache_manage, kernels/expert_cache.hip:592-603, then expert_cache_gather,
+ * :626-643).  It has no counterpart symbol in the reference library; the reference names
+ * launch count as the per-layer cost it fused against (expert_cache.hip:316-330). */
+EXPERT_CACHE_API int expert_cache_step(
+    const int* topk_ids, int mk, int E, int S, int max_distinct, int max_inserts, int* table,
+    int* map_cold, int* slot_expert, long long* slot_stamp, unsigned char* routed,
+    long long* step, int* miss, int* n_miss, int policy, int decay, void* out_ids,
+    int out_elem_bytes, void* d0, const void* s0, long b0, void* d1, const void* s1, long b1,
+    void* d2, const void* s2, long b2, void* d3, const void* s3, long b3, void* d4,
+    const void* s4, long b4, void* d5, const void* s5, long b5, int chunks, int lanes,
+    int* sync, int max_wait_us, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -119,6 +119,25 @@ def test_gather_refuses_bad_grid_and_alignment(h):
     assert gather(h, [16] * 6, ptr=8) == -1
 
 
+def step(h, E=8, S=4, mi=4, policy=0, mk=2, out=True, elem=4, sizes=(16,) * 6, ptr=256,
+         chunks=16, lanes=64, sync=512, wait=0):
+    buf = ctypes.c_void_p(1024) if out else NULL
+    trip = []
+    for b in sizes:
+        trip += [ctypes.c_void_p(ptr), ctypes.c_void_p(ptr), ctypes.c_long(b)]
+    return h.expert_cache_step(NULL, mk, E, S, 8, mi, *([NULL] * 8), policy, 64, buf, elem,
+                               *trip, chunks, lanes, ctypes.c_void_p(sync), wait, NULL)
+
+
+@pytest.mark.parametrize("kw", [dict(E=0), dict(S=0), dict(S=257), dict(mi=1025),
+                                dict(policy=2), dict(out=False), dict(elem=2),
+                                dict(sizes=(16,) * 5 + (24,)), dict(ptr=8), dict(chunks=0),
+                                dict(lanes=-1), dict(sync=0), dict(sync=514), dict(wait=-1)])
+def test_step_refuses_bad_arguments(h, kw):
+    # refused before any CUDA call: these return -1 on a machine without a GPU
+    assert step(h, **kw) == -1
+
+
 def test_library_search_order(monkeypatch, tmp_path):
     from vllm_expert_cache import _lib
     fake = tmp_path / "libexpertcache.so"

@@ -498,19 +498,23 @@ __device__ __forceinline__ uint4 load_stream(const uint4* p) {
   return r;
 }
 
-__global__ void __launch_bounds__(kGatherThreads)
-    gather_kernel(const __grid_constant__ GatherArgs a) {
+// Copy tiles u = first, first + stride, ... of the flattened work of `nm` misses.  With
+// kCoherent the miss list is read from L2 (it was written earlier in the same launch);
+// otherwise a previous launch wrote it and plain loads are fine.
+template <bool kCoherent>
+__device__ __forceinline__ void gather_tiles(const GatherArgs& a, int nm, long long first_u,
+                                             long long stride) {
   const int per_miss = a.tile_start[a.nbuf];
-  grid_dependency_wait();   // the miss list is written by the manage launch before us
-  const long long total = (long long)a.n_miss[0] * per_miss;
-  for (long long u = blockIdx.x; u < total; u += gridDim.x) {
+  const long long total = (long long)nm * per_miss;
+  for (long long u = first_u; u < total; u += stride) {
     const int j = (int)(u / per_miss);
     const int v = (int)(u - (long long)j * per_miss);
     int k = 0;
     while (v >= a.tile_start[k + 1]) ++k;
     const long long first = (long long)(v - a.tile_start[k]) * kTileVecs;
     const long long left = a.vecs[k] - first;
-    const long long e = a.miss[2 * j], s = a.miss[2 * j + 1];
+    const long long e = kCoherent ? __ldcg(a.miss + 2 * j) : a.miss[2 * j];
+    const long long s = kCoherent ? __ldcg(a.miss + 2 * j + 1) : a.miss[2 * j + 1];
     const uint4* src = a.src[k] + e * a.vecs[k] + first;
     uint4* dst = a.dst[k] + s * a.vecs[k] + first;
     uint4 r[kGatherUnroll];
@@ -524,6 +528,100 @@ __global__ void __launch_bounds__(kGatherThreads)
       const int x = threadIdx.x + i * kGatherThreads;
       if (x < left) dst[x] = r[i];
     }
+  }
+}
+
+__global__ void __launch_bounds__(kGatherThreads)
+    gather_kernel(const __grid_constant__ GatherArgs a) {
+  grid_dependency_wait();   // the miss list is written by the manage launch before us
+  gather_tiles<false>(a, a.n_miss[0], blockIdx.x, gridDim.x);
+}
+
+// ---------------------------------------------------------------------------------------
+// step: manage + remap + gather in one launch (expert_cache_step)
+//
+// A decode step that installs nothing then costs one graph node instead of two.  Every CTA
+// takes a ticket from sync[0] on entry; the first to arrive (ticket 0) is running, so it
+// runs the policy step and the remap, then releases sync[2].  The others wait for that
+// flag -- with a time bound -- and then all CTAs copy the miss list's tiles.  Because the
+// manager is whichever CTA arrived first, no CTA ever waits on one that has not been
+// scheduled.  The last CTA to leave clears sync[0..2] for the next launch; sync[3] counts
+// CTAs whose wait ran out (they copy nothing), and sync[4..5] (int64) counts installs; the
+// kernel never clears either.
+
+constexpr int kStepThreads = kGatherThreads;
+
+struct StepArgs {
+  ManageArgs m;
+  GatherArgs g;
+  int* sync;               // [8] arrivals, departures, ready, timed-out waits, installs
+                           // (int64 at [4]), reserved
+  long long wait_ns;       // bound on a CTA's wait for the policy step
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int load_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void store_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_constant__ StepArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ int s_ticket, s_go;
+  const int t = threadIdx.x;
+  grid_dependency_wait();     // ids (and the previous launch's counters) are final
+  if (t == 0) s_ticket = atomicAdd(&a.sync[0], 1);
+  __syncthreads();
+  int nm = 0;
+  if (s_ticket == 0) {
+    const ManageSmem sm = manage_smem(smem, a.m.E, a.m.S);
+    const int my_id = (t < a.m.mk) ? a.m.ids[t] : -1;
+    manage_core<kStepThreads>(a.m, sm, my_id);
+    __threadfence();          // installs and the miss list, before the release below
+    __syncthreads();          // also publishes the installs' table updates in sm.table
+    if (t == 0) store_release_gpu(&a.sync[2], 1);
+    if (a.m.out_ids)
+      remap_tail(a.m.ids, a.m.mk, a.m.E, a.m.out_ids, a.m.out_elem_bytes, sm.table, my_id,
+                 kStepThreads);
+    nm = __ldcg(a.g.n_miss);
+    // running install count: only this CTA writes it, and launches sharing `sync` are
+    // stream-ordered
+    if (t == 0) *reinterpret_cast<long long*>(a.sync + 4) += nm;
+  } else {
+    if (t == 0) {
+      const unsigned long long t0 = global_ns();
+      unsigned ns = 32;
+      int ok = 0;
+      for (long long it = 0; it < (1LL << 26); ++it) {
+        if (load_acquire_gpu(&a.sync[2]) != 0) {
+          ok = 1;
+          break;
+        }
+        if ((long long)(global_ns() - t0) > a.wait_ns) break;
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
+      }
+      if (!ok) atomicAdd(&a.sync[3], 1);
+      s_go = ok;
+    }
+    __syncthreads();
+    if (s_go) nm = __ldcg(a.g.n_miss);
+  }
+  gather_tiles<true>(a.g, nm, blockIdx.x, gridDim.x);
+  if (t == 0 && atomicAdd(&a.sync[1], 1) == (int)gridDim.x - 1) {
+    a.sync[0] = 0;            // every CTA has arrived and left: reset for the next launch
+    a.sync[2] = 0;
+    a.sync[1] = 0;
   }
 }
 
@@ -614,21 +712,27 @@ int current_device() {
   return d;
 }
 
-// Opt each manage instantiation into the full shared-memory carve-out once per device.
-template <int NT>
-cudaError_t ensure_manage_smem(int dev) {
-  static std::atomic<bool> done[kMaxDevices];
+// Opt a kernel into the full shared-memory carve-out once per device (`done` is the
+// kernel's own per-device flag array).
+template <typename Kernel>
+cudaError_t ensure_smem_optin(Kernel fn, std::atomic<bool>* done, int dev) {
   if (done[dev].load(std::memory_order_acquire)) return cudaSuccess;
   int optin = 0;
   cudaError_t err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (err != cudaSuccess) return err;
   cudaFuncAttributes fa{};
-  err = cudaFuncGetAttributes(&fa, manage_kernel<NT>);
+  err = cudaFuncGetAttributes(&fa, fn);
   if (err != cudaSuccess) return err;
-  err = cudaFuncSetAttribute(manage_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)fa.sharedSizeBytes);
   if (err == cudaSuccess) done[dev].store(true, std::memory_order_release);
   return err;
+}
+
+template <int NT>
+cudaError_t ensure_manage_smem(int dev) {
+  static std::atomic<bool> done[kMaxDevices];
+  return ensure_smem_optin(manage_kernel<NT>, done, dev);
 }
 
 template <int NT>
@@ -668,11 +772,15 @@ int launch_fused(const ManageArgs& a, const AlignArgs& g, cudaStream_t stream) {
   return (int)cudaLaunchKernelEx(&cfg, fused_kernel<NT>, a, g);
 }
 
+bool manage_args_ok(const ManageArgs& a) {
+  if (a.E <= 0 || a.E > EXPERT_CACHE_MAX_EXPERTS) return false;
+  if (a.S <= 0 || a.S > EXPERT_CACHE_MAX_SLOTS || a.S > (1 << kSlotBits) - 1) return false;
+  if (a.max_inserts < 0 || a.max_inserts > EXPERT_CACHE_MAX_INSERTS) return false;
+  return a.policy == 0 || a.policy == 1;
+}
+
 int manage_checked(const ManageArgs& a, cudaStream_t stream) {
-  if (a.E <= 0 || a.E > EXPERT_CACHE_MAX_EXPERTS) return -1;
-  if (a.S <= 0 || a.S > EXPERT_CACHE_MAX_SLOTS || a.S > (1 << kSlotBits) - 1) return -1;
-  if (a.max_inserts < 0 || a.max_inserts > EXPERT_CACHE_MAX_INSERTS) return -1;
-  if (a.policy < 0 || a.policy > 1) return -1;
+  if (!manage_args_ok(a)) return -1;
   if (a.S <= 128) return launch_manage<128>(a, stream);
   if (a.S <= 256) return launch_manage<256>(a, stream);
   return launch_manage<1024>(a, stream);
@@ -710,6 +818,79 @@ ManageArgs make_manage_args(const int* topk_ids, int mk, int E, int S, int max_d
 
 // SM count per device, looked up once (sizes the gather grid).
 std::atomic<int> g_sm_count[kMaxDevices];
+
+// The six (dst, src, bytes) triples of one gather as kernel arguments: -1 on a refused
+// triple.  A triple repeated from an earlier one (the caller's padding) is copied once.
+int make_gather_args(void* const* dsts, const void* const* srcs, const long* bytes,
+                     const int* miss, const int* n_miss, GatherArgs* out) {
+  for (int i = 0; i < EXPERT_CACHE_GATHER_SLOTS; ++i) {
+    if (bytes[i] <= 0 || bytes[i] % 16) return -1;
+    if ((reinterpret_cast<uintptr_t>(dsts[i]) | reinterpret_cast<uintptr_t>(srcs[i])) & 15)
+      return -1;
+  }
+  GatherArgs a{};
+  int n = 0;
+  long long tiles = 0;
+  a.tile_start[0] = 0;
+  for (int i = 0; i < EXPERT_CACHE_GATHER_SLOTS; ++i) {
+    bool repeat = false;
+    for (int k = 0; k < i; ++k)
+      repeat |= dsts[k] == dsts[i] && srcs[k] == srcs[i] && bytes[k] == bytes[i];
+    if (repeat) continue;
+    a.dst[n] = static_cast<uint4*>(dsts[i]);
+    a.src[n] = static_cast<const uint4*>(srcs[i]);
+    a.vecs[n] = bytes[i] / 16;
+    tiles += (a.vecs[n] + kTileVecs - 1) / kTileVecs;
+    if (tiles > INT_MAX / 2) return -1;
+    a.tile_start[n + 1] = (int)tiles;
+    ++n;
+  }
+  a.nbuf = n;
+  a.miss = miss;
+  a.n_miss = n_miss;
+  *out = a;
+  return 0;
+}
+
+// chunks * lanes is the CTA budget; more than two CTAs per SM never moved bytes faster
+// (the host link is the bound), and an idle launch (no misses) retires sooner small.
+int gather_grid(int chunks, int lanes, unsigned* grid) {
+  if (chunks <= 0 || lanes <= 0) return -1;
+  const int dev = current_device();
+  if (dev < 0) return (int)cudaErrorInvalidDevice;
+  int sms = g_sm_count[dev].load(std::memory_order_relaxed);
+  if (sms == 0) {
+    const cudaError_t err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return (int)err;
+    g_sm_count[dev].store(sms, std::memory_order_relaxed);
+  }
+  const long long budget = (long long)chunks * (long long)lanes;
+  const long long cap = (long long)kGatherCtasPerSm * sms;
+  *grid = (unsigned)(budget < cap ? budget : cap);
+  return 0;
+}
+
+int launch_step(const StepArgs& a, unsigned grid, cudaStream_t stream) {
+  const size_t smem = manage_smem_bytes(a.m.E, a.m.S);
+  if (smem > 48 * 1024) {
+    static std::atomic<bool> done[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0) return (int)cudaErrorInvalidDevice;
+    const cudaError_t err = ensure_smem_optin(step_kernel, done, dev);
+    if (err != cudaSuccess) return (int)err;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, step_kernel, a);
+}
 
 // Device address of g_noalloc_routed on the current device, looked up once per device.
 std::atomic<void*> g_noalloc_routed_addr[kMaxDevices];
@@ -802,6 +983,37 @@ int expert_cache_manage_remap_noalloc(const int* topk_ids, int mk, int E, int S,
                                    policy, decay, out_ids, out_elem_bytes, stream);
 }
 
+int expert_cache_step(const int* topk_ids, int mk, int E, int S, int max_distinct,
+                      int max_inserts, int* table, int* map_cold, int* slot_expert,
+                      long long* slot_stamp, unsigned char* routed, long long* step, int* miss,
+                      int* n_miss, int policy, int decay, void* out_ids, int out_elem_bytes,
+                      void* d0, const void* s0, long b0, void* d1, const void* s1, long b1,
+                      void* d2, const void* s2, long b2, void* d3, const void* s3, long b3,
+                      void* d4, const void* s4, long b4, void* d5, const void* s5, long b5,
+                      int chunks, int lanes, int* sync, int max_wait_us, cudaStream_t stream) {
+  if ((out_ids == nullptr && mk > 0) || (out_elem_bytes != 4 && out_elem_bytes != 8))
+    return -1;
+  if (sync == nullptr || (reinterpret_cast<uintptr_t>(sync) & 7) || max_wait_us < 0) return -1;
+  if (S > EXPERT_CACHE_STEP_MAX_SLOTS) return -1;
+  StepArgs a{};
+  a.m = make_manage_args(topk_ids, mk, E, S, max_distinct, max_inserts, table, map_cold,
+                         slot_expert, slot_stamp, routed, step, miss, n_miss, policy, decay);
+  a.m.out_ids = mk > 0 ? out_ids : nullptr;
+  a.m.out_elem_bytes = out_elem_bytes;
+  if (!manage_args_ok(a.m)) return -1;
+  void* dsts[EXPERT_CACHE_GATHER_SLOTS] = {d0, d1, d2, d3, d4, d5};
+  const void* srcs[EXPERT_CACHE_GATHER_SLOTS] = {s0, s1, s2, s3, s4, s5};
+  const long bytes[EXPERT_CACHE_GATHER_SLOTS] = {b0, b1, b2, b3, b4, b5};
+  int rc = make_gather_args(dsts, srcs, bytes, miss, n_miss, &a.g);
+  if (rc != 0) return rc;
+  unsigned grid = 0;
+  rc = gather_grid(chunks, lanes, &grid);
+  if (rc != 0) return rc;
+  a.sync = sync;
+  a.wait_ns = 1000LL * (max_wait_us > 0 ? max_wait_us : EXPERT_CACHE_STEP_DEFAULT_WAIT_US);
+  return launch_step(a, grid, stream);
+}
+
 int expert_cache_manage_ep(const int* topk_ids, int mk, const int* expert_map, int E_global,
                            int E, int S, int max_distinct, int max_inserts, int* table,
                            int* map_cold, int* slot_expert, long long* slot_stamp,
@@ -859,48 +1071,14 @@ int expert_cache_gather(void* d0, const void* s0, long b0, void* d1, const void*
   void* dsts[EXPERT_CACHE_GATHER_SLOTS] = {d0, d1, d2, d3, d4, d5};
   const void* srcs[EXPERT_CACHE_GATHER_SLOTS] = {s0, s1, s2, s3, s4, s5};
   const long bytes[EXPERT_CACHE_GATHER_SLOTS] = {b0, b1, b2, b3, b4, b5};
-  for (int i = 0; i < EXPERT_CACHE_GATHER_SLOTS; ++i) {
-    if (bytes[i] <= 0 || bytes[i] % 16) return -1;
-    if ((reinterpret_cast<uintptr_t>(dsts[i]) | reinterpret_cast<uintptr_t>(srcs[i])) & 15)
-      return -1;
-  }
-  if (chunks <= 0 || lanes <= 0) return -1;
-
   GatherArgs a{};
-  int n = 0;
-  long long tiles = 0;
-  a.tile_start[0] = 0;
-  for (int i = 0; i < EXPERT_CACHE_GATHER_SLOTS; ++i) {
-    bool repeat = false;   // the caller pads to six by repeating a triple: copy it once
-    for (int k = 0; k < i; ++k)
-      repeat |= dsts[k] == dsts[i] && srcs[k] == srcs[i] && bytes[k] == bytes[i];
-    if (repeat) continue;
-    a.dst[n] = static_cast<uint4*>(dsts[i]);
-    a.src[n] = static_cast<const uint4*>(srcs[i]);
-    a.vecs[n] = bytes[i] / 16;
-    tiles += (a.vecs[n] + kTileVecs - 1) / kTileVecs;
-    if (tiles > INT_MAX / 2) return -1;
-    a.tile_start[n + 1] = (int)tiles;
-    ++n;
-  }
-  a.nbuf = n;
-  a.miss = miss;
-  a.n_miss = n_miss;
-
-  // chunks * lanes is the CTA budget; more than two CTAs per SM never moved bytes faster
-  // (the host link is the bound), and an idle launch (no misses) retires sooner small.
-  long long grid = (long long)chunks * (long long)lanes;
-  const int dev = current_device();
-  if (dev < 0) return (int)cudaErrorInvalidDevice;
-  int sms = g_sm_count[dev].load(std::memory_order_relaxed);
-  if (sms == 0) {
-    const cudaError_t err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (err != cudaSuccess) return (int)err;
-    g_sm_count[dev].store(sms, std::memory_order_relaxed);
-  }
-  grid = grid < (long long)kGatherCtasPerSm * sms ? grid : (long long)kGatherCtasPerSm * sms;
+  int rc = make_gather_args(dsts, srcs, bytes, miss, n_miss, &a);
+  if (rc != 0) return rc;
+  unsigned grid = 0;
+  rc = gather_grid(chunks, lanes, &grid);
+  if (rc != 0) return rc;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)grid);
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kGatherThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;

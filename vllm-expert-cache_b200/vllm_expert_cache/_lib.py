@@ -4,7 +4,7 @@ Search order, as in the reference (vllm_expert_cache/_lib.py:17-33): $EXPERT_CAC
 then ``libexpertcache.so`` beside this package, then /usr/local/lib.  A missing library
 raises FileNotFoundError; there is no fallback path.  The handle is loaded once per
 process.  Argument types are the reference's (_lib.py:41-53) plus the fused-remap,
-expert-parallel and prefetch entry points this build adds.
+expert-parallel, prefetch and single-launch step entry points this build adds.
 """
 
 from __future__ import annotations
@@ -15,6 +15,8 @@ from pathlib import Path
 
 # Six (dst, src, bytes) triples per gather call (reference _lib.py:61).
 GATHER_SLOTS = 6
+# Largest slot count of the single-launch step (EXPERT_CACHE_STEP_MAX_SLOTS).
+STEP_MAX_SLOTS = 256
 
 _P, _I, _L = ctypes.c_void_p, ctypes.c_int, ctypes.c_long
 MANAGE_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P]
@@ -23,6 +25,8 @@ MANAGE_EP_ARGTYPES = [_P, _I, _P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P, _P]
 PREFETCH_ARGTYPES = [_P] + [_I] * 5 + [_P] * 8 + [_I, _P]
 PREGATE_ARGTYPES = [_P, _I, _I, _I, _P, _I, _I, _P, _P]
 GATHER_ARGTYPES = [_P, _P, _L] * GATHER_SLOTS + [_P, _P, _I, _I, _P]
+STEP_ARGTYPES = ([_P] + [_I] * 5 + [_P] * 8 + [_I] * 2 + [_P, _I] + [_P, _P, _L] * GATHER_SLOTS
+                 + [_I, _I, _P, _I, _P])
 
 _handle = None
 
@@ -56,6 +60,8 @@ def bind(h: ctypes.CDLL) -> ctypes.CDLL:
     h.expert_cache_pregate.argtypes = PREGATE_ARGTYPES
     h.expert_cache_gather.restype = _I
     h.expert_cache_gather.argtypes = GATHER_ARGTYPES
+    h.expert_cache_step.restype = _I
+    h.expert_cache_step.argtypes = STEP_ARGTYPES
     return h
 
 

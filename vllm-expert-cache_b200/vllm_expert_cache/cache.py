@@ -2,13 +2,17 @@
 
 The full expert tensors stay where vLLM's offloader put them (pinned host memory seen by
 the GPU through UVA); this class adds ``S`` device-resident slots per expert tensor and
-the policy state that decides which experts occupy them.  One cached forward step is:
+the policy state that decides which experts occupy them.  One cached forward step is one
+``expert_cache_step`` launch (S <= 256):
 
-  1. ``expert_cache_manage_remap`` (one CTA): policy step on the routed ids -- hits
-     refreshed, victims chosen among slots this step does not need, table / miss list
-     rewritten -- and, in the same launch, the routing ids remapped expert -> slot;
-  2. ``expert_cache_gather``: every missing expert's slabs copied from host memory into
-     its new slot (six tensors per launch; wider sets take several launches).
+  1. its first CTA runs the policy step on the routed ids -- hits refreshed, victims
+     chosen among slots this step does not need, table / miss list rewritten -- and
+     remaps the routing ids expert -> slot;
+  2. then all its CTAs copy every missing expert's slabs from host memory into their new
+     slots (six tensors per launch; a wider set adds ``expert_cache_gather`` launches).
+
+With more than 256 slots the same step is two launches, ``expert_cache_manage_remap``
+then ``expert_cache_gather``.
 
 Nothing reads a device value back, so the step is recorded into CUDA graphs like any
 other kernel sequence; every rank that sees the same routing evolves the same state.
@@ -25,7 +29,7 @@ import ctypes
 
 import torch
 
-from ._lib import GATHER_SLOTS, lib
+from ._lib import GATHER_SLOTS, STEP_MAX_SLOTS, lib
 from .config import settings
 
 
@@ -82,6 +86,9 @@ class ExpertSlotCache:
         self.step = torch.zeros((1,), dtype=torch.int64, device=dev)
         self.miss = torch.zeros((2 * self.S,), dtype=torch.int32, device=dev)
         self.n_miss = torch.zeros((1,), dtype=torch.int32, device=dev)
+        # expert_cache_step's launch counters, its count of timed-out waits and its
+        # running install count (int64 at [4])
+        self.sync = torch.zeros((8,), dtype=torch.int32, device=dev)
 
         # Opt-in counter: installs summed over every cached step (device int64, no sync).
         self.miss_total = (torch.zeros((1,), dtype=torch.int64, device=dev)
@@ -140,14 +147,22 @@ class ExpertSlotCache:
         wide = topk_ids.dtype in (torch.int32, torch.int64)
         out = torch.empty(topk_ids.shape, dtype=topk_ids.dtype if wide else torch.int32,
                           device=self.device)
-        rc = h.expert_cache_manage_remap(
-            _ptr(ids), mk, self.E, self.S, min(self.E, mk), self.S, *self._state(),
-            self.policy, self.decay, _ptr(out), out.element_size(), stream)
-        if rc != 0:
-            raise RuntimeError(f"expert_cache_manage_remap failed rc={rc}")
-        if self.miss_total is not None:
-            self.miss_total.add_(self.n_miss)
-        self._gather(h, stream)
+        args = (_ptr(ids), mk, self.E, self.S, min(self.E, mk), self.S, *self._state(),
+                self.policy, self.decay, _ptr(out), out.element_size())
+        if self.S <= STEP_MAX_SLOTS:
+            groups = self._gather_groups()
+            rc = h.expert_cache_step(*args, *groups[0], self.chunks, self.lanes,
+                                     _ptr(self.sync), 0, stream)
+            if rc != 0:
+                raise RuntimeError(f"expert_cache_step failed rc={rc}")
+            self._gather(h, stream, groups[1:])
+        else:
+            rc = h.expert_cache_manage_remap(*args, stream)
+            if rc != 0:
+                raise RuntimeError(f"expert_cache_manage_remap failed rc={rc}")
+            self._gather(h, stream)
+            if self.miss_total is not None:     # the step kernel counts its own installs
+                self.miss_total.add_(self.n_miss)
         return out if wide else out.to(topk_ids.dtype)
 
     def refresh_ep(self, topk_ids: torch.Tensor, expert_map: torch.Tensor) -> torch.Tensor:
@@ -210,26 +225,43 @@ class ExpertSlotCache:
 
     def stats(self) -> dict:
         """Host snapshot of the counters (synchronises; call outside the hot path)."""
-        out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item())}
-        if self.miss_total is not None:
-            out["installs"] = int(self.miss_total.item())
-            if self.prefetch_total is not None:
-                out["prefetch_installs"] = int(self.prefetch_total.item())
+        sync = self.sync.cpu()
+        step_installs = int(sync[4:6].view(torch.int64)[0])
+        out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item()),
+               "step_timeouts": int(sync[3])}
+        if self.S <= STEP_MAX_SLOTS or self.miss_total is not None:
+            # the single-launch step counts installs itself; the two-launch path (S > 256,
+            # EP steps) only with EXPERT_CACHE_STATS=1
+            other = int(self.miss_total.item()) if self.miss_total is not None else 0
+            out["installs"] = step_installs + other
             out["bytes_per_install"] = sum(_bytes_per_expert(getattr(self.owner, n).data)
                                            for n in self.names)
+        if self.prefetch_total is not None:
+            out["prefetch_installs"] = int(self.prefetch_total.item())
         return out
 
-    def _gather(self, h, stream) -> None:
+    def step_timeouts(self) -> int:
+        """CTAs of ``expert_cache_step`` whose wait for the policy step ran out, summed over
+        every call (0 in normal operation; synchronises, so call it outside the hot path)."""
+        return int(self.sync[3].item())
+
+    def _gather_groups(self) -> list[list]:
+        """The (dst, src, bytes) arguments of every gather launch, six triples each."""
         triples = []
         for name in self.names:
             src = getattr(self.owner, name).data
             triples.append((_ptr(self.slots[name]), _ptr(src),
                             ctypes.c_long(_bytes_per_expert(src))))
+        groups = []
         for i in range(0, len(triples), GATHER_SLOTS):
             group = triples[i:i + GATHER_SLOTS]
             # pad with the group's last triple: the kernel copies a repeated triple once
             group += [group[-1]] * (GATHER_SLOTS - len(group))
-            args = [x for tr in group for x in tr]
+            groups.append([x for tr in group for x in tr])
+        return groups
+
+    def _gather(self, h, stream, groups=None) -> None:
+        for args in (self._gather_groups() if groups is None else groups):
             rc = h.expert_cache_gather(*args, _ptr(self.miss), _ptr(self.n_miss),
                                        self.chunks, self.lanes, stream)
             if rc != 0:
