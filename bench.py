@@ -352,7 +352,7 @@ class Layer:
             raise RuntimeError(f"expert_cache_step rc={rc}")
 
     def timeouts(self) -> int:
-        return int(self.sync[3].item())
+        return int(self.sync[5].item())
 
 
 def plan_trace(layer: Layer, steps, misses, tokens, seed):
@@ -704,7 +704,7 @@ def step_graphs(layer, trace, cold, reps=2):
     start()
     graphs["step"].replay()
     torch.cuda.synchronize()
-    installs = int(layer.sync[4:6].cpu().view(torch.int64)[0])
+    installs = int(layer.sync[6:8].cpu().view(torch.int64)[0])
     same = all(torch.equal(finals["step"][k], finals["two_launch"][k]) for k in finals["step"])
     timeouts = layer.timeouts()
     del graphs

@@ -70,7 +70,14 @@ MIXTRAL_8X7B = {
     "torch_dtype": "bfloat16", "use_cache": True, "vocab_size": 32000,
 }
 
-MODELS = {"qwen3-30b-a3b": (QWEN3_30B_A3B, 151936), "mixtral-8x7b": (MIXTRAL_8X7B, 32000)}
+# the Qwen3-235B-A22B shape (94 layers; runs here truncated with
+# --layers so that the offloaded experts fit the host's pinned memory).
+QWEN3_235B_A22B = dict(QWEN3_30B_A3B, hidden_size=4096, num_attention_heads=64,
+                       num_key_value_heads=4, moe_intermediate_size=1536,
+                       intermediate_size=12288, num_hidden_layers=94, max_window_layers=94)
+
+MODELS = {"qwen3-30b-a3b": (QWEN3_30B_A3B, 151936), "mixtral-8x7b": (MIXTRAL_8X7B, 32000),
+          "qwen3-235b-a22b": (QWEN3_235B_A22B, 151936)}
 
 W8A8_INT8 = {  # int8 weights + dynamic per-token int8 activations
     "quant_method": "compressed-tensors", "format": "int-quantized",
@@ -176,8 +183,13 @@ def init_synthetic_weights(model, std: float = 0.02) -> None:
 
 
 def cache_stats_on_worker(worker) -> list:
-    """collective_rpc target: every armed layer's counters (EXPERT_CACHE_STATS=1), the
-    tensors it mirrors and every name bound to slot storage during a cached step."""
+    """collective_rpc target: every armed layer's counters, the tensors it mirrors, every
+    name bound to slot storage during a cached step, a digest of its policy state (equal
+    on every tensor-parallel rank when the ranks stayed in step) and a consistency check
+    of that state (table[e] = s exactly when slot_expert[s] = e)."""
+    import hashlib
+
+    import numpy as np
     model = worker.model_runner.get_model()
     out = []
     for m in model.modules():
@@ -188,6 +200,16 @@ def cache_stats_on_worker(worker) -> list:
             st["bound"] = sorted(c.bound)
             st["method"] = type(m.quant_method).__name__
             st["prefetch_linked"] = c.next is not None
+            table, se = c.table.cpu().numpy(), c.slot_expert.cpu().numpy()
+            h = hashlib.blake2b(digest_size=8)
+            for t in (table, c.map_cold.cpu().numpy(), se, c.slot_stamp.cpu().numpy(),
+                      c.step.cpu().numpy()):
+                h.update(np.ascontiguousarray(t).tobytes())
+            st["state_digest"] = h.hexdigest()
+            occupied = se >= 0
+            st["consistent"] = bool(
+                all(table[e] == s for s, e in enumerate(se) if e >= 0) and
+                int((table >= 0).sum()) == int(occupied.sum()))
             out.append(st)
     return out
 
@@ -335,6 +357,8 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
         env[ROUTING_ENV] = mode["routing"]
     if mode.get("split"):
         env["EXPERT_CACHE_SPLIT_WIDE"] = str(mode["split"])
+    env["EXPERT_CACHE_EP"] = "1" if args.ep else "0"
+    env["EXPERT_CACHE_SINGLE_LAUNCH"] = "0" if mode.get("two_launch") else "1"
     if args.deterministic:
         env["VLLM_BATCH_INVARIANT"] = "1"   # vLLM's deterministic (batch-invariant) kernels
     # the counters are fetched with collective_rpc(<function>), which vLLM pickles
@@ -345,7 +369,9 @@ def run_mode(mode: dict, args, model_dir: Path, site: Path, logdir: Path) -> dic
            "--prompt", str(args.prompt), "--gen", str(args.gen), "--seed", str(args.seed),
            "--batch", str(args.batch), "--vocab", str(MODELS[args.arch][1]),
            "--gpu-util", str(args.gpu_util), "--moe-backend", args.moe_backend,
-           "--temperature", str(args.temperature)]
+           "--temperature", str(args.temperature), "--reps", str(args.reps)]
+    if args.ep:
+        cmd.append("--ep")
     if args.parity_batch:
         cmd.append("--parity-batch")
     if args.no_autotune or args.deterministic:
@@ -376,13 +402,15 @@ def child(mode: dict, a) -> None:
     kw = dict(model=a.model, skip_tokenizer_init=True, load_format=LOAD_FORMAT,
               dtype="bfloat16", tensor_parallel_size=a.tp, max_model_len=a.prompt + a.gen + 16,
               gpu_memory_utilization=a.gpu_util, max_num_seqs=a.batch, seed=a.seed,
-              enable_prefix_caching=False)
+              enable_prefix_caching=False, disable_log_stats=False)
     if a.moe_backend != "auto":
         kw["moe_backend"] = a.moe_backend
     if a.no_autotune:
         kw["enable_flashinfer_autotune"] = False
     if mode.get("offload"):
         kw.update(cpu_offload_gb=mode["offload_gb"], cpu_offload_params={"experts"})
+    if a.ep:
+        kw["enable_expert_parallel"] = True
     t0 = time.time()
     llm = LLM(**kw)
     init_s = time.time() - t0
@@ -417,18 +445,28 @@ def child(mode: dict, a) -> None:
             v = sorted((float(x.logprob) for x in d.values()), reverse=True)
             gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
     times = {}
+    engine_decode = []
     for n in (1, a.gen):
         best = None
-        for _ in range(2):
+        for _ in range(a.reps):
             if mode.get("routing"):
                 llm.collective_rpc(reset_routing_on_worker)
             t = time.perf_counter()
-            llm.generate(prompts, SamplingParams(max_tokens=n, **timed), use_tqdm=False)
+            outs = llm.generate(prompts, SamplingParams(max_tokens=n, **timed), use_tqdm=False)
             dt = time.perf_counter() - t
             best = dt if best is None else min(best, dt)
+            if n == a.gen:
+                # the engine's own clock: first token (end of prefill) to last token
+                ts = [(o.metrics.first_token_ts, o.metrics.last_token_ts) for o in outs
+                      if getattr(o, "metrics", None) is not None]
+                if len(ts) == len(outs) and all(b > a_ for a_, b in ts):
+                    engine_decode.append(max(b for _, b in ts) - min(a_ for a_, _ in ts))
         times[n] = best
-    # decode tokens of the whole batch per second of decode (prefill time removed)
-    decode_tps = a.batch * (a.gen - 1) / (times[a.gen] - times[1])
+    # decode tokens of the whole batch per second of decode: timed by the engine between
+    # each request's first and last token (no prefill in it); the wall-clock difference
+    # t(gen) - t(1) is kept beside it
+    wall_tps = a.batch * (a.gen - 1) / (times[a.gen] - times[1])
+    decode_tps = (a.batch * (a.gen - 1) / min(engine_decode)) if engine_decode else wall_tps
     cache = None
     if mode.get("slots"):
         per_rank = llm.collective_rpc(cache_stats_on_worker)
@@ -441,6 +479,11 @@ def child(mode: dict, a) -> None:
                      "method": layers[0]["method"],
                      "step_wait_timeouts": sum(x.get("step_timeouts", 0) for x in layers)}
             cache["prefetch_linked"] = sum(bool(x.get("prefetch_linked")) for x in layers)
+            cache["consistent"] = all(x["consistent"] for r in per_rank for x in r)
+            cache["ranks"] = len(per_rank)
+            cache["ranks_identical"] = all(
+                [x["state_digest"] for x in r] == [x["state_digest"] for x in layers]
+                for r in per_rank)
             if "installs" in layers[0]:
                 cache.update(installs=installs,
                              installs_per_layer_step=round(installs / max(steps, 1), 4),
@@ -453,8 +496,10 @@ def child(mode: dict, a) -> None:
            "prefetch": mode.get("prefetch") or 0, "routing": mode.get("routing") or "model",
            "policy": mode.get("policy") or a.policy,
            "offload": bool(mode.get("offload")),
-           "tp": a.tp, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
+           "tp": a.tp, "ep": a.ep, "batch": a.batch, "init_s": round(init_s, 1), "prefill_s": round(times[1], 4),
            "gen_s": round(times[a.gen], 4), "decode_tok_s": round(decode_tps, 2),
+           "decode_tok_s_wall": round(wall_tps, 2),
+           "decode_timer": "engine first-to-last token" if engine_decode else "wall t(gen)-t(1)",
            "cache": cache, "tokens": tokens, "logprobs": lps, "gaps": gaps}
     print(json.dumps({"decode_result": out}), flush=True)
 
@@ -467,6 +512,9 @@ def parser() -> argparse.ArgumentParser:
     ap.add_argument("--gpu-util", type=float, default=0.55)
     ap.add_argument("--vocab", type=int, default=151936)
     ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--ep", action="store_true",
+                    help="vLLM expert parallelism across the TP ranks "
+                         "(--enable-expert-parallel); cached modes set EXPERT_CACHE_EP=1")
     ap.add_argument("--slots", type=int, nargs="*", default=[16, 32, 64, 96])
     ap.add_argument("--prompt", type=int, default=128)
     ap.add_argument("--gen", type=int, default=512)
@@ -513,8 +561,13 @@ def parser() -> argparse.ArgumentParser:
     ap.add_argument("--prefetch", type=int, nargs="*", default=[],
                     help="EXPERT_CACHE_PREFETCH values (predictions per token, 0 = off): "
                          "every slot count runs once per value")
+    ap.add_argument("--launch", nargs="*", default=["single"], choices=["single", "two"],
+                    help="cached step form: one expert_cache_step launch, or two launches "
+                         "(EXPERT_CACHE_SINGLE_LAUNCH=0); every slot count runs once per value")
     ap.add_argument("--parity-batch", action="store_true",
                     help="greedy parity run over the whole batch instead of its first prompt")
+    ap.add_argument("--reps", type=int, default=2, help="timed generations per length; the "
+                    "best is kept")
     ap.add_argument("--mode-timeout", type=int, default=1200)
     ap.add_argument("--budget-s", type=float, default=0,
                     help="stop starting new modes once this much wall time has passed "
@@ -544,12 +597,15 @@ def plan_modes(a) -> list[dict]:
             for sl in a.slots:
                 for v in (a.split_wide or [0]):
                     for f in (a.prefetch or [0]):
-                        name = (f"slots{sl}" + (f"-{pol}" if pol else "") +
-                                (f"-split{v}" if v else "") + (f"-prefetch{f}" if f else "") +
-                                tag)
-                        modes.append({"name": name, "slots": sl, "split": v, "prefetch": f,
-                                      "policy": pol, "offload": True,
-                                      "offload_gb": a.offload_gb, **extra})
+                        for launch in a.launch:
+                            name = (f"slots{sl}" + (f"-{pol}" if pol else "") +
+                                    (f"-split{v}" if v else "") +
+                                    (f"-prefetch{f}" if f else "") +
+                                    ("-two-launch" if launch == "two" else "") + tag)
+                            modes.append({"name": name, "slots": sl, "split": v,
+                                          "prefetch": f, "policy": pol, "offload": True,
+                                          "two_launch": launch == "two",
+                                          "offload_gb": a.offload_gb, **extra})
     return modes
 
 

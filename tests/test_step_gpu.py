@@ -7,12 +7,14 @@
 * The same drive through ``expert_cache_step`` and through the two launches it replaces
   (``expert_cache_manage_remap`` then ``expert_cache_gather``) at the Qwen3-30B-A3B W8A8
   slab: identical state, slot ids and slot bytes.
-* A CUDA graph of many step nodes replayed; the launch counters return to zero after
-  every launch and no wait ever runs out.
-* The wait bound: with the arrival counter pre-set so that no CTA becomes the policy CTA
-  (a flag nothing sets), every CTA's wait runs out, is counted in sync[3], and changes
-  nothing; the next call is correct again.  No GPU fault is involved: the wait is a bounded
-  poll that returns.
+* A CUDA graph of many step nodes replayed (every replayed node is a new grid, so each
+  elects its own policy CTA); no wait ever runs out and the install count is exact.
+* The wait bound: with a 1 us bound and a policy step that takes far longer (E = 32768,
+  2048 routing ids), the other CTAs' waits run out and are counted in sync[5]; the policy
+  CTA then copies every tile alone, so state, remap and slot bytes are still exact.  Stale
+  words from earlier launches (sync left as a previous call wrote it, or filled with
+  garbage) are never taken for the current launch's.  No GPU fault is involved: the wait
+  is a bounded poll that returns.
 All comparisons are bit-exact.
 """
 
@@ -87,9 +89,9 @@ def nins_of(st, ids, md, mi, E):
 
 
 def counters(sync):
-    """(arrivals, departures, ready, timed-out waits), installs."""
+    """(timed-out waits, installs) from a step's sync array."""
     c = sync.cpu()
-    return c[:4].tolist(), int(c[4:6].view(torch.int64)[0])
+    return int(c[5]), int(c[6:8].view(torch.int64)[0])
 
 
 def drive(h, E, S, mk, mi, md, pol, decay, steps, rng, sizes=(48, 32, 16), chunks=16,
@@ -124,7 +126,7 @@ def drive(h, E, S, mk, mi, md, pol, decay, steps, rng, sizes=(48, 32, 16), chunk
                                           err_msg=f"{tag} t{t}: remap")
         slabs.check(pairs, f"{tag} t{t}")
         installs += len(pairs)
-        assert counters(sync) == ([0, 0, 0, 0], installs), tag
+        assert counters(sync) == (0, installs), tag
     # every occupied slot holds its expert at the end
     slabs.check([(int(e), s) for s, e in enumerate(ds.slot_expert.cpu().numpy()) if e >= 0],
                 tag)
@@ -230,39 +232,58 @@ def test_graph_of_many_steps(h):
         np.testing.assert_array_equal(got_out[t], policy.remap(st.table, trace[t]))
     compare_state(ds.host(), st, 0, "after graph")
     slabs.check([(int(e), s) for s, e in enumerate(st.slot_expert) if e >= 0], "graph")
-    assert counters(sync) == ([0, 0, 0, 0], int(got_nm.sum()))
+    assert counters(sync) == (0, int(got_nm.sum()))
 
 
-def test_wait_bound_runs_out_and_is_reported(h):
-    """No CTA takes ticket 0, so nobody runs the policy step: every wait runs out after
-    max_wait_us, is counted in sync[3], and nothing else changes.  The counters are reset
-    on the way out, so the next call is an ordinary step."""
-    E, S, mk = 64, 16, 8
+def test_wait_bound_runs_out_and_no_bytes_are_lost(h):
+    """1 us wait bound against a slow policy step: waits run out, the result is exact."""
+    rng = np.random.default_rng(17)
+    E, S, mk = 32768, 256, 2048
+    st = policy.CacheState(E, S, miss_cap=S)
+    ds = DeviceState(st)
+    slabs = Slabs(E, S, (4096, 48), seed=12)
+    sync = torch.zeros(8, dtype=torch.int32, device=DEV)
+    out = torch.empty(mk, dtype=torch.int32, device=DEV)
+    timed_out = installs = 0
+    for t in range(4):
+        ids = rng.choice(E, size=mk, replace=False).astype(np.int32)
+        nins = nins_of(st, ids, 10 ** 6, S, E)
+        pairs = policy.manage(st, ids, 10 ** 6, S, 1, 64)
+        step(h, ds, torch.from_numpy(ids).to(DEV), 10 ** 6, S, 1, 64, out, slabs, sync,
+             wait_us=1)
+        torch.cuda.synchronize()
+        compare_state(ds.host(), st, nins, f"t{t}")
+        np.testing.assert_array_equal(out.cpu().numpy(), policy.remap(st.table, ids))
+        slabs.check(pairs, f"t{t}")
+        installs += len(pairs)
+        timed_out, got_installs = counters(sync)
+        assert got_installs == installs
+    assert timed_out > 0, "no wait ran out: the bound was not exercised"
+
+
+def test_stale_sync_words_are_never_taken_for_the_current_launch(h):
+    """sync filled with garbage (and then left as each call wrote it): every launch still
+    elects one policy CTA and publishes under its own grid id."""
+    from synthetic import sticky_zipf_trace
+    E, S = 128, 16
     st = policy.CacheState(E, S)
     ds = DeviceState(st)
-    slabs = Slabs(E, S, (256,), seed=8)
-    sync = torch.tensor([1, 0, 0, 0, 0, 0, 0, 0], dtype=torch.int32, device=DEV)  # stale arrival
-    ids = torch.arange(mk, dtype=torch.int32, device=DEV)
-    out = torch.full((mk,), -7, dtype=torch.int32, device=DEV)
-    before = ds.host()
-    chunks, lanes = 2, 3                       # 6 CTAs
-    step(h, ds, ids, mk, S, 1, 64, out, slabs, sync, chunks, lanes, wait_us=2000)
-    torch.cuda.synchronize()
-    assert counters(sync) == ([0, 0, 0, chunks * lanes], 0)
-    after = ds.host()
-    for f in ("table", "map_cold", "slot_expert", "slot_stamp", "routed", "step", "n_miss"):
-        np.testing.assert_array_equal(after[f], before[f], err_msg=f)
-    assert (out.cpu() == -7).all()             # the remap did not run either
-    for d in slabs.dsts:
-        assert int(d.count_nonzero()) == 0
-    # the next call is ordinary; the timeout count stays as a record
-    pairs = policy.manage(st, ids.cpu().numpy(), mk, S, 1, 64)
-    step(h, ds, ids, mk, S, 1, 64, out, slabs, sync, chunks, lanes)
-    torch.cuda.synchronize()
-    compare_state(ds.host(), st, len(pairs), "after timeout")
-    np.testing.assert_array_equal(out.cpu().numpy(), policy.remap(st.table, ids.cpu().numpy()))
-    slabs.check(pairs, "after timeout")
-    assert counters(sync) == ([0, 0, 0, chunks * lanes], len(pairs))
+    slabs = Slabs(E, S, (512, 64), seed=13)
+    # owner 7, a ready word with n_miss 3 under a tag no grid of this process reaches, a
+    # tile counter of 99
+    garbage = torch.tensor([7, 0, 3, 0x7FFFFFFF, 99, 0, 0, 0], dtype=torch.int32)
+    sync = garbage.to(DEV)
+    out = torch.empty(8, dtype=torch.int32, device=DEV)
+    trace = sticky_zipf_trace(11, steps=40, E=E)
+    for t in range(len(trace)):
+        nins = nins_of(st, trace[t], 8, S, E)
+        pairs = policy.manage(st, trace[t], 8, S, 0, 0)
+        step(h, ds, torch.from_numpy(trace[t]).to(DEV), 8, S, 0, 0, out, slabs, sync)
+        torch.cuda.synchronize()
+        compare_state(ds.host(), st, nins, f"t{t}")
+        np.testing.assert_array_equal(out.cpu().numpy(), policy.remap(st.table, trace[t]))
+        slabs.check(pairs, f"t{t}")
+    assert int(sync[5].item()) == 0
 
 
 def test_refresh_beyond_step_slots_uses_two_launches(monkeypatch):

@@ -138,15 +138,37 @@ __device__ __forceinline__ ManageSmem manage_smem(unsigned char* base, int E, in
   return m;
 }
 
+// The one round of loads of a policy step: table, routed flags and slot state into shared
+// memory (no barrier).  Returns the step counter as read before this call advances it.
+// Flag bits: 1 = routed by this call's ids; 2 = routed by the previous step (prefetch
+// only: those slots are parked, not installed).
+template <int NT>
+__device__ __forceinline__ long long manage_stage(const ManageArgs& a, const ManageSmem& sm) {
+  const int t = threadIdx.x;
+  const long long step0 = a.step[0];
+  for (int e = t; e < a.E; e += NT) {
+    sm.table[e] = a.table[e];
+    sm.flag[e] = (a.prefetch && a.routed[e]) ? 2 : 0;
+  }
+  for (int s = t; s < a.S; s += NT) {
+    sm.slot_expert[s] = a.slot_expert[s];
+    sm.stamp[s] = a.slot_stamp[s];
+  }
+  return step0;
+}
+
 // One policy step for the whole CTA (NT threads, S <= NT).  Thread t owns slot t; experts
 // are processed in tiles of NT (thread t owns expert base + t), in ascending id.  All
 // global state is read once into shared memory and written back directly.  On return
 // `sm.table` holds the updated expert->slot table, but only for the installing threads'
 // own writes: the caller needs a CTA barrier before reading it when this returns true
-// (true = installs happened).  `my_id` is topk_ids[t] (or -1 when t >= mk).
+// (true = installs happened).  `my_id` is topk_ids[t] (or -1 when t >= mk).  With
+// `staged`, manage_stage already ran and a CTA barrier followed it; `step0` is its value.
+// `n_out`, when given, receives n_miss in thread 0.
 template <int NT>
 __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSmem& sm,
-                                            int my_id) {
+                                            int my_id, bool staged = false,
+                                            long long step0 = 0, int* n_out = nullptr) {
   constexpr int NW = NT / 32;
   __shared__ int s_missing[EXPERT_CACHE_MAX_INSERTS];   // r-th missing expert, ascending
   __shared__ int w_routed[2][NW], w_missed[2][NW], w_evict[NW];
@@ -162,18 +184,11 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
   const int t = threadIdx.x, lane = t & 31, w = t >> 5;
 
   // ---- one round of loads: step, table, slot state (ids were read by the caller) -------
-  const long long now = a.step[0] + (a.prefetch ? 0 : 1);
-  // Flag bits: 1 = routed by this call's ids; 2 = routed by the previous step (prefetch
-  // only: those slots are parked, not installed).
-  for (int e = t; e < E; e += NT) {
-    s_tab[e] = a.table[e];
-    s_flag[e] = (a.prefetch && a.routed[e]) ? 2 : 0;
+  if (!staged) {
+    step0 = manage_stage<NT>(a, sm);
+    __syncthreads();
   }
-  for (int s = t; s < S; s += NT) {
-    s_se[s] = a.slot_expert[s];
-    s_st[s] = a.slot_stamp[s];
-  }
-  __syncthreads();
+  const long long now = step0 + (a.prefetch ? 0 : 1);
   if (t == 0 && !a.prefetch) a.step[0] = now;   // every thread read the old value above
 
   // ---- routed flags (every writer of an entry stores the same value) -------------------
@@ -242,6 +257,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
     // keep their refreshed priority and no ageing runs (it only runs on inserting steps).
     if (!read_through && hit) a.slot_stamp[t] = stamp;
     if (t == 0) a.n_miss[0] = 0;
+    if (t == 0 && n_out) *n_out = 0;
     return false;
   }
 
@@ -295,6 +311,7 @@ __device__ __forceinline__ bool manage_core(const ManageArgs& a, const ManageSme
     }
   }
   if (t == 0) a.n_miss[0] = min(nins, n_evict);
+  if (t == 0 && n_out) *n_out = min(nins, n_evict);
   return true;
 }
 
@@ -540,24 +557,44 @@ __global__ void __launch_bounds__(kGatherThreads)
 // ---------------------------------------------------------------------------------------
 // step: manage + remap + gather in one launch (expert_cache_step)
 //
-// A decode step that installs nothing then costs one graph node instead of two.  Every CTA
-// takes a ticket from sync[0] on entry; the first to arrive (ticket 0) is running, so it
-// runs the policy step and the remap, then releases sync[2].  The others wait for that
-// flag -- with a time bound -- and then all CTAs copy the miss list's tiles.  Because the
-// manager is whichever CTA arrived first, no CTA ever waits on one that has not been
-// scheduled.  The last CTA to leave clears sync[0..2] for the next launch; sync[3] counts
-// CTAs whose wait ran out (they copy nothing), and sync[4..5] (int64) counts installs; the
-// kernel never clears either.
+// A decode step that installs nothing is then one graph node instead of two.  Each launch
+// identifies itself by its grid id (%gridid: unique per grid launch in a context, the same
+// for all its CTAs), so no counter has to be reset between launches and nothing a
+// previous launch left behind can be mistaken for this one's:
+//
+//   - election: every CTA swaps the grid id into `owner`; the one that finds another
+//     value there arrived first -- it is running -- and runs the policy step and remap;
+//   - publication: it resets this launch's tile counter, then publishes
+//     (grid id << 20 | n_miss) in one release store; the other CTAs wait for a word with
+//     their grid id (bounded);
+//   - copy: every participating CTA claims 32 KiB tiles of the miss list's copy from the
+//     tile counter until none are left.  The policy CTA claims tiles too, so it alone
+//     completes the copy if no other CTA ever sees the word: a wait that runs out
+//     (counted, never silent) costs time, never bytes.
+// While thread 0 swaps, every thread already stages the state into shared memory (small
+// E only), so the swap's round trip overlaps the state load.
+//
+// sync (int32[8], 8-byte aligned, zero before first use): [0..1] owner grid id + 1 (u64),
+// [2..3] ready word (u64), [4] tile counter of the current launch, [5] running count of
+// waits that ran out, [6..7] running install count (u64).
 
 constexpr int kStepThreads = kGatherThreads;
+constexpr int kStepStageMaxExperts = 4096;   // stage speculatively up to this E
+constexpr int kReadyShift = 20;              // n_miss <= 1024 < 2^20
 
 struct StepArgs {
   ManageArgs m;
   GatherArgs g;
-  int* sync;               // [8] arrivals, departures, ready, timed-out waits, installs
-                           // (int64 at [4]), reserved
+  int* sync;
   long long wait_ns;       // bound on a CTA's wait for the policy step
+  int chunks, lanes;       // CTA budget (host side only)
 };
+
+__device__ __forceinline__ unsigned long long grid_id() {
+  unsigned long long g;
+  asm volatile("mov.u64 %0, %%gridid;" : "=l"(g));
+  return g;
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -565,63 +602,99 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-__device__ __forceinline__ int load_acquire_gpu(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long load_acquire_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void store_release_gpu(int* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void store_release_gpu(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void copy_tile(const GatherArgs& a, int per_miss, long long u) {
+  const int j = (int)(u / per_miss);
+  const int v = (int)(u - (long long)j * per_miss);
+  int k = 0;
+  while (v >= a.tile_start[k + 1]) ++k;
+  const long long first = (long long)(v - a.tile_start[k]) * kTileVecs;
+  const long long left = a.vecs[k] - first;
+  const long long e = __ldcg(a.miss + 2 * j), s = __ldcg(a.miss + 2 * j + 1);
+  const uint4* src = a.src[k] + e * a.vecs[k] + first;
+  uint4* dst = a.dst[k] + s * a.vecs[k] + first;
+  uint4 r[kGatherUnroll];
+#pragma unroll
+  for (int i = 0; i < kGatherUnroll; ++i) {
+    const int x = threadIdx.x + i * kGatherThreads;
+    if (x < left) r[i] = load_stream(src + x);
+  }
+#pragma unroll
+  for (int i = 0; i < kGatherUnroll; ++i) {
+    const int x = threadIdx.x + i * kGatherThreads;
+    if (x < left) dst[x] = r[i];
+  }
 }
 
 __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_constant__ StepArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_ticket, s_go;
+  __shared__ int s_manager, s_nm, s_tile;
   const int t = threadIdx.x;
-  grid_dependency_wait();     // ids (and the previous launch's counters) are final
-  if (t == 0) s_ticket = atomicAdd(&a.sync[0], 1);
+  unsigned long long* owner = reinterpret_cast<unsigned long long*>(a.sync);
+  unsigned long long* ready = owner + 1;
+  int* tile_ctr = a.sync + 4;
+  const unsigned long long gid = grid_id() + 1;          // never 0, the initial contents
+  const unsigned long long tag = gid & ((1ull << (64 - kReadyShift)) - 1);
+  grid_dependency_wait();     // ids and state are final
+  if (t == 0) s_manager = atomicExch(owner, gid) != gid;
+  const ManageSmem sm = manage_smem(smem, a.m.E, a.m.S);
+  const int my_id = (t < a.m.mk) ? a.m.ids[t] : -1;
+  const bool staged = a.m.E <= kStepStageMaxExperts;
+  long long step0 = 0;
+  if (staged) step0 = manage_stage<kStepThreads>(a.m, sm);   // overlaps the swap
   __syncthreads();
   int nm = 0;
-  if (s_ticket == 0) {
-    const ManageSmem sm = manage_smem(smem, a.m.E, a.m.S);
-    const int my_id = (t < a.m.mk) ? a.m.ids[t] : -1;
-    manage_core<kStepThreads>(a.m, sm, my_id);
-    __threadfence();          // installs and the miss list, before the release below
-    __syncthreads();          // also publishes the installs' table updates in sm.table
-    if (t == 0) store_release_gpu(&a.sync[2], 1);
+  if (s_manager) {
+    manage_core<kStepThreads>(a.m, sm, my_id, staged, step0, &s_nm);
+    if (t == 0) *tile_ctr = 0;          // this launch's tiles start at 0
+    __syncthreads();                    // installs, miss list, n_miss and table complete
+    nm = s_nm;
+    if (t == 0) store_release_gpu(ready, (tag << kReadyShift) | (unsigned long long)nm);
     if (a.m.out_ids)
       remap_tail(a.m.ids, a.m.mk, a.m.E, a.m.out_ids, a.m.out_elem_bytes, sm.table, my_id,
                  kStepThreads);
-    nm = __ldcg(a.g.n_miss);
-    // running install count: only this CTA writes it, and launches sharing `sync` are
-    // stream-ordered
-    if (t == 0) *reinterpret_cast<long long*>(a.sync + 4) += nm;
+    // running install count: only the policy CTA writes it, launches are stream-ordered
+    if (t == 0) *reinterpret_cast<long long*>(a.sync + 6) += nm;
   } else {
     if (t == 0) {
       const unsigned long long t0 = global_ns();
       unsigned ns = 32;
-      int ok = 0;
+      int got = -1;
       for (long long it = 0; it < (1LL << 26); ++it) {
-        if (load_acquire_gpu(&a.sync[2]) != 0) {
-          ok = 1;
+        const unsigned long long v = load_acquire_gpu(ready);
+        if ((v >> kReadyShift) == tag) {
+          got = (int)(v & ((1ull << kReadyShift) - 1));
           break;
         }
         if ((long long)(global_ns() - t0) > a.wait_ns) break;
         __nanosleep(ns);
         if (ns < 256) ns <<= 1;
       }
-      if (!ok) atomicAdd(&a.sync[3], 1);
-      s_go = ok;
+      if (got < 0) atomicAdd(a.sync + 5, 1);
+      s_nm = got < 0 ? 0 : got;
     }
     __syncthreads();
-    if (s_go) nm = __ldcg(a.g.n_miss);
+    nm = s_nm;
   }
-  gather_tiles<true>(a.g, nm, blockIdx.x, gridDim.x);
-  if (t == 0 && atomicAdd(&a.sync[1], 1) == (int)gridDim.x - 1) {
-    a.sync[0] = 0;            // every CTA has arrived and left: reset for the next launch
-    a.sync[2] = 0;
-    a.sync[1] = 0;
+  if (nm == 0) return;
+  const int per_miss = a.g.tile_start[a.g.nbuf];
+  const long long total = (long long)nm * per_miss;
+  for (;;) {
+    if (t == 0) s_tile = atomicAdd(tile_ctr, 1);
+    __syncthreads();
+    const long long u = s_tile;
+    __syncthreads();
+    if (u >= total) break;
+    copy_tile(a.g, per_miss, u);
   }
 }
 
@@ -870,7 +943,7 @@ int gather_grid(int chunks, int lanes, unsigned* grid) {
   return 0;
 }
 
-int launch_step(const StepArgs& a, unsigned grid, cudaStream_t stream) {
+int launch_step(const StepArgs& a, cudaStream_t stream) {
   const size_t smem = manage_smem_bytes(a.m.E, a.m.S);
   if (smem > 48 * 1024) {
     static std::atomic<bool> done[kMaxDevices];
@@ -879,6 +952,9 @@ int launch_step(const StepArgs& a, unsigned grid, cudaStream_t stream) {
     const cudaError_t err = ensure_smem_optin(step_kernel, done, dev);
     if (err != cudaSuccess) return (int)err;
   }
+  unsigned grid = 0;
+  const int rc = gather_grid(a.chunks, a.lanes, &grid);
+  if (rc != 0) return rc;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kStepThreads);
@@ -1006,12 +1082,12 @@ int expert_cache_step(const int* topk_ids, int mk, int E, int S, int max_distinc
   const long bytes[EXPERT_CACHE_GATHER_SLOTS] = {b0, b1, b2, b3, b4, b5};
   int rc = make_gather_args(dsts, srcs, bytes, miss, n_miss, &a.g);
   if (rc != 0) return rc;
-  unsigned grid = 0;
-  rc = gather_grid(chunks, lanes, &grid);
-  if (rc != 0) return rc;
+  if (chunks <= 0 || lanes <= 0) return -1;
+  a.chunks = chunks;
+  a.lanes = lanes;
   a.sync = sync;
   a.wait_ns = 1000LL * (max_wait_us > 0 ? max_wait_us : EXPERT_CACHE_STEP_DEFAULT_WAIT_US);
-  return launch_step(a, grid, stream);
+  return launch_step(a, stream);
 }
 
 int expert_cache_manage_ep(const int* topk_ids, int mk, const int* expert_map, int E_global,

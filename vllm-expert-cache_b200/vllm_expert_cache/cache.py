@@ -11,8 +11,8 @@ the policy state that decides which experts occupy them.  One cached forward ste
   2. then all its CTAs copy every missing expert's slabs from host memory into their new
      slots (six tensors per launch; a wider set adds ``expert_cache_gather`` launches).
 
-With more than 256 slots the same step is two launches, ``expert_cache_manage_remap``
-then ``expert_cache_gather``.
+With more than 256 slots (or EXPERT_CACHE_SINGLE_LAUNCH=0) the same step is two launches,
+``expert_cache_manage_remap`` then ``expert_cache_gather``.
 
 Nothing reads a device value back, so the step is recorded into CUDA graphs like any
 other kernel sequence; every rank that sees the same routing evolves the same state.
@@ -86,8 +86,8 @@ class ExpertSlotCache:
         self.step = torch.zeros((1,), dtype=torch.int64, device=dev)
         self.miss = torch.zeros((2 * self.S,), dtype=torch.int32, device=dev)
         self.n_miss = torch.zeros((1,), dtype=torch.int32, device=dev)
-        # expert_cache_step's launch counters, its count of timed-out waits and its
-        # running install count (int64 at [4])
+        # expert_cache_step's per-launch words, its count of timed-out waits ([5]) and its
+        # running install count (int64 at [6])
         self.sync = torch.zeros((8,), dtype=torch.int32, device=dev)
 
         # Opt-in counter: installs summed over every cached step (device int64, no sync).
@@ -115,6 +115,7 @@ class ExpertSlotCache:
         self.decay = settings.decay
         self.chunks = settings.chunks
         self.lanes = settings.lanes
+        self.single_launch = settings.single_launch and self.S <= STEP_MAX_SLOTS
         self._state_args = None
 
     # ---------------------------------------------------------------------------------
@@ -149,7 +150,7 @@ class ExpertSlotCache:
                           device=self.device)
         args = (_ptr(ids), mk, self.E, self.S, min(self.E, mk), self.S, *self._state(),
                 self.policy, self.decay, _ptr(out), out.element_size())
-        if self.S <= STEP_MAX_SLOTS:
+        if self.single_launch:
             groups = self._gather_groups()
             rc = h.expert_cache_step(*args, *groups[0], self.chunks, self.lanes,
                                      _ptr(self.sync), 0, stream)
@@ -226,12 +227,12 @@ class ExpertSlotCache:
     def stats(self) -> dict:
         """Host snapshot of the counters (synchronises; call outside the hot path)."""
         sync = self.sync.cpu()
-        step_installs = int(sync[4:6].view(torch.int64)[0])
+        step_installs = int(sync[6:8].view(torch.int64)[0])
         out = {"experts": self.E, "slots": self.S, "steps": int(self.step.item()),
-               "step_timeouts": int(sync[3])}
-        if self.S <= STEP_MAX_SLOTS or self.miss_total is not None:
+               "step_timeouts": int(sync[5])}
+        if self.single_launch or self.miss_total is not None:
             # the single-launch step counts installs itself; the two-launch path (S > 256,
-            # EP steps) only with EXPERT_CACHE_STATS=1
+            # EXPERT_CACHE_SINGLE_LAUNCH=0, EP steps) only with EXPERT_CACHE_STATS=1
             other = int(self.miss_total.item()) if self.miss_total is not None else 0
             out["installs"] = step_installs + other
             out["bytes_per_install"] = sum(_bytes_per_expert(getattr(self.owner, n).data)
@@ -243,7 +244,7 @@ class ExpertSlotCache:
     def step_timeouts(self) -> int:
         """CTAs of ``expert_cache_step`` whose wait for the policy step ran out, summed over
         every call (0 in normal operation; synchronises, so call it outside the hot path)."""
-        return int(self.sync[3].item())
+        return int(self.sync[5].item())
 
     def _gather_groups(self) -> list[list]:
         """The (dst, src, bytes) arguments of every gather launch, six triples each."""

@@ -28,6 +28,9 @@ cache.py:96-97, _lib.py:18, README.md:103-116):
                                   previous layer's MoE input and installs the top N
                                   predicted experts per token on a side stream while that
                                   layer computes (new, off by default)
+  EXPERT_CACHE_SINGLE_LAUNCH 1    '1': a cached step with S <= 256 is one
+                                  expert_cache_step launch; '0': two launches (manage +
+                                  remap, then gather), the form used above 256 slots (new)
 
 ``slots_for(E)`` clamps to [1, E]: EXPERT_CACHE_SLOTS=0 means one slot, not "off".
 """
@@ -96,6 +99,10 @@ class Settings:
     @property
     def prefetch(self) -> int:
         return max(0, int(_env("EXPERT_CACHE_PREFETCH", "0") or 0))
+
+    @property
+    def single_launch(self) -> bool:
+        return _env("EXPERT_CACHE_SINGLE_LAUNCH", "1") != "0"
 
     def slots_for(self, num_experts: int) -> int:
         want = self.slots
