@@ -912,6 +912,7 @@ def _decode_view(r: dict | None) -> dict | None:
            "init_s": r.get("init_s"), "wall_s": r.get("wall_s")}
     if cache:
         out.update(installs_per_layer_step=cache.get("installs_per_layer_step"),
+                   timed_installs_per_layer_step=cache.get("timed_installs_per_layer_step"),
                    layer_steps=cache.get("layer_steps"), installs=cache.get("installs"),
                    armed_layers=cache.get("armed_layers"),
                    step_wait_timeouts=cache.get("step_wait_timeouts"))

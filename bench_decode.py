@@ -444,6 +444,15 @@ def child(mode: dict, a) -> None:
         for d in ref.logprobs:
             v = sorted((float(x.logprob) for x in d.values()), reverse=True)
             gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
+    def installs_now():
+        if not mode.get("slots"):
+            return None
+        ranks = llm.collective_rpc(cache_stats_on_worker)
+        layers = ranks[0] if ranks else []
+        return (sum(x.get("installs", 0) for x in layers),
+                sum(x["steps"] for x in layers))
+
+    before = installs_now()
     times = {}
     engine_decode = []
     for n in (1, a.gen):
@@ -465,6 +474,7 @@ def child(mode: dict, a) -> None:
     # decode tokens of the whole batch per second of decode: timed by the engine between
     # each request's first and last token (no prefill in it); the wall-clock difference
     # t(gen) - t(1) is kept beside it
+    after = installs_now()
     wall_tps = a.batch * (a.gen - 1) / (times[a.gen] - times[1])
     decode_tps = (a.batch * (a.gen - 1) / min(engine_decode)) if engine_decode else wall_tps
     cache = None
@@ -484,6 +494,10 @@ def child(mode: dict, a) -> None:
             cache["ranks_identical"] = all(
                 [x["state_digest"] for x in r] == [x["state_digest"] for x in layers]
                 for r in per_rank)
+            if before is not None and after is not None and after[1] > before[1]:
+                # only the timed generations (their prefills read through and add no steps)
+                cache["timed_installs_per_layer_step"] = round(
+                    (after[0] - before[0]) / (after[1] - before[1]), 4)
             if "installs" in layers[0]:
                 cache.update(installs=installs,
                              installs_per_layer_step=round(installs / max(steps, 1), 4),
