@@ -265,20 +265,20 @@ EXPERT_CACHE_API int expert_cache_gather(void* d0, const void* s0, long b0, void
  *
  * A decode step that installs nothing is then one kernel node instead of two.  Inside the
  * launch, the first CTA to start runs the policy step and the remap and publishes the
- * miss count in a device word tagged with the launch's own grid id; the other CTAs wait
- * for that word (bounded by max_wait_us, 0 = EXPERT_CACHE_STEP_DEFAULT_WAIT_US) and then
- * every CTA claims 32 KiB tiles of the slabs' copy until none are left.  The policy CTA
- * copies too, so it completes the copy alone if the others never see the word: a wait
- * that runs out costs time, never bytes.
+ * miss count in a device word tagged with the launch's epoch; the other CTAs wait for
+ * that word (bounded by max_wait_us, 0 = EXPERT_CACHE_STEP_DEFAULT_WAIT_US) and then every
+ * CTA claims 32 KiB tiles of the slabs' copy until none are left.  The policy CTA copies
+ * too, so it completes the copy alone if the others never see the word: a wait that runs
+ * out costs time, never bytes.
  *
  *   sync   [8] int32 (8-byte aligned), zero before the first call and then owned by these
- *          calls: [0..1] the grid id of the last launch that elected its policy CTA,
- *          [2..3] the tagged miss-count word, [4] the current launch's tile counter,
- *          [5] a running count of CTAs whose wait ran out, [6..7] a running int64 count
- *          of installed experts (the sum of n_miss over calls).  Nothing in it has to be
- *          reset between calls; a launch never reads a word another launch wrote as its
- *          own.  Use one sync array per cache (per layer); launches sharing one must be
- *          ordered on one stream.
+ *          calls: [0..1] the arrival word (epoch, CTAs arrived), which the last CTA of a
+ *          launch moves to the next epoch, [2..3] the tagged miss-count word, [4] the
+ *          current launch's tile counter, [5] a running count of CTAs whose wait ran out,
+ *          [6..7] a running int64 count of installed experts (the sum of n_miss over
+ *          calls).  Nothing has to be reset between calls, including CUDA-graph replays
+ *          of one captured call.  Use one sync array per cache (per layer); launches
+ *          sharing one must be ordered on one stream.
  *
  * Returns -1 on the rules of expert_cache_manage_remap and expert_cache_gather, when
  * S > EXPERT_CACHE_STEP_MAX_SLOTS, when sync is NULL or not 8-byte aligned, or when

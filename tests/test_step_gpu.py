@@ -7,14 +7,13 @@
 * The same drive through ``expert_cache_step`` and through the two launches it replaces
   (``expert_cache_manage_remap`` then ``expert_cache_gather``) at the Qwen3-30B-A3B W8A8
   slab: identical state, slot ids and slot bytes.
-* A CUDA graph of many step nodes replayed (every replayed node is a new grid, so each
-  elects its own policy CTA); no wait ever runs out and the install count is exact.
+* A CUDA graph of many step nodes replayed once, and a graph of one step node replayed
+  many times (each replay is a new epoch of the same node); no wait ever runs out and
+  the install count is exact.
 * The wait bound: with a 1 us bound and a policy step that takes far longer (E = 32768,
   2048 routing ids), the other CTAs' waits run out and are counted in sync[5]; the policy
-  CTA then copies every tile alone, so state, remap and slot bytes are still exact.  Stale
-  words from earlier launches (sync left as a previous call wrote it, or filled with
-  garbage) are never taken for the current launch's.  No GPU fault is involved: the wait
-  is a bounded poll that returns.
+  CTA then copies every tile alone, so state, remap and slot bytes are still exact.  No
+  GPU fault is involved: the wait is a bounded poll that returns.
 All comparisons are bit-exact.
 """
 
@@ -261,29 +260,39 @@ def test_wait_bound_runs_out_and_no_bytes_are_lost(h):
     assert timed_out > 0, "no wait ran out: the bound was not exercised"
 
 
-def test_stale_sync_words_are_never_taken_for_the_current_launch(h):
-    """sync filled with garbage (and then left as each call wrote it): every launch still
-    elects one policy CTA and publishes under its own grid id."""
+def test_one_node_replayed_many_times(h):
+    """One captured step node replayed 300 times with new ids each time: every replay must
+    elect its own policy CTA and never take an earlier replay's published word."""
     from synthetic import sticky_zipf_trace
     E, S = 128, 16
     st = policy.CacheState(E, S)
     ds = DeviceState(st)
-    slabs = Slabs(E, S, (512, 64), seed=13)
-    # owner 7, a ready word with n_miss 3 under a tag no grid of this process reaches, a
-    # tile counter of 99
-    garbage = torch.tensor([7, 0, 3, 0x7FFFFFFF, 99, 0, 0, 0], dtype=torch.int32)
-    sync = garbage.to(DEV)
+    slabs = Slabs(E, S, (1024, 64), seed=13)
+    sync = torch.zeros(8, dtype=torch.int32, device=DEV)
+    ids = torch.zeros(8, dtype=torch.int32, device=DEV)
     out = torch.empty(8, dtype=torch.int32, device=DEV)
-    trace = sticky_zipf_trace(11, steps=40, E=E)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        step(h, ds, ids, 8, S, 0, 0, out, slabs, sync)
+    torch.cuda.synchronize()
+    trace = sticky_zipf_trace(11, steps=300, E=E)
+    installs = 0
     for t in range(len(trace)):
+        ids.copy_(torch.from_numpy(trace[t]))
+        g.replay()
         nins = nins_of(st, trace[t], 8, S, E)
         pairs = policy.manage(st, trace[t], 8, S, 0, 0)
-        step(h, ds, torch.from_numpy(trace[t]).to(DEV), 8, S, 0, 0, out, slabs, sync)
-        torch.cuda.synchronize()
-        compare_state(ds.host(), st, nins, f"t{t}")
-        np.testing.assert_array_equal(out.cpu().numpy(), policy.remap(st.table, trace[t]))
-        slabs.check(pairs, f"t{t}")
-    assert int(sync[5].item()) == 0
+        installs += len(pairs)
+        if pairs or t % 25 == 24:
+            torch.cuda.synchronize()
+            compare_state(ds.host(), st, nins, f"t{t}")
+            np.testing.assert_array_equal(out.cpu().numpy(), policy.remap(st.table, trace[t]))
+            slabs.check(pairs, f"t{t}")
+    torch.cuda.synchronize()
+    assert counters(sync) == (0, installs)
 
 
 def test_refresh_beyond_step_slots_uses_two_launches(monkeypatch):

@@ -557,24 +557,27 @@ __global__ void __launch_bounds__(kGatherThreads)
 // ---------------------------------------------------------------------------------------
 // step: manage + remap + gather in one launch (expert_cache_step)
 //
-// A decode step that installs nothing is then one graph node instead of two.  Each launch
-// identifies itself by its grid id (%gridid: unique per grid launch in a context, the same
-// for all its CTAs), so no counter has to be reset between launches and nothing a
-// previous launch left behind can be mistaken for this one's:
+// A decode step that installs nothing is then one graph node instead of two.  A launch
+// tells its own words from a previous launch's by an epoch kept in the arrival word
+// (high 32 bits: epoch, low 32 bits: CTAs arrived in this epoch):
 //
-//   - election: every CTA swaps the grid id into `owner`; the one that finds another
-//     value there arrived first -- it is running -- and runs the policy step and remap;
-//   - publication: it resets this launch's tile counter, then publishes
-//     (grid id << 20 | n_miss) in one release store; the other CTAs wait for a word with
-//     their grid id (bounded);
-//   - copy: every participating CTA claims 32 KiB tiles of the miss list's copy from the
-//     tile counter until none are left.  The policy CTA claims tiles too, so it alone
-//     completes the copy if no other CTA ever sees the word: a wait that runs out
-//     (counted, never silent) costs time, never bytes.
-// While thread 0 swaps, every thread already stages the state into shared memory (small
-// E only), so the swap's round trip overlaps the state load.
+//   - election: every CTA adds 1 to the arrival word and gets (epoch, ticket).  Ticket 0
+//     arrived first -- it is running -- and runs the policy step and the remap.  The CTA
+//     that draws ticket G - 1 arrived last; it moves the word to (epoch + 1, 0), so the
+//     next launch (or graph replay) starts a new epoch with every counter of this one
+//     behind it.  Nothing waits for that: every CTA of this launch already holds its
+//     ticket.
+//   - publication: the policy CTA resets the tile counter, then publishes
+//     ((epoch + 1) << 20 | n_miss) in one release store; the other CTAs wait for a word
+//     with their epoch (bounded).
+//   - copy: every CTA claims 32 KiB tiles of the miss list's copy from the tile counter
+//     until none are left.  The policy CTA claims tiles too, so it alone completes the
+//     copy if no other CTA ever sees the word: a wait that runs out (counted, never
+//     silent) costs time, never bytes.
+// While thread 0 takes its ticket, every thread already stages the state into shared
+// memory (small E only), so the ticket's round trip overlaps the state load.
 //
-// sync (int32[8], 8-byte aligned, zero before first use): [0..1] owner grid id + 1 (u64),
+// sync (int32[8], 8-byte aligned, zero before first use): [0..1] arrival word (u64),
 // [2..3] ready word (u64), [4] tile counter of the current launch, [5] running count of
 // waits that ran out, [6..7] running install count (u64).
 
@@ -589,12 +592,6 @@ struct StepArgs {
   long long wait_ns;       // bound on a CTA's wait for the policy step
   int chunks, lanes;       // CTA budget (host side only)
 };
-
-__device__ __forceinline__ unsigned long long grid_id() {
-  unsigned long long g;
-  asm volatile("mov.u64 %0, %%gridid;" : "=l"(g));
-  return g;
-}
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -637,23 +634,29 @@ __device__ __forceinline__ void copy_tile(const GatherArgs& a, int per_miss, lon
 
 __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_constant__ StepArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int s_manager, s_nm, s_tile;
+  __shared__ unsigned long long s_arrival;
+  __shared__ int s_nm, s_tile;
   const int t = threadIdx.x;
-  unsigned long long* owner = reinterpret_cast<unsigned long long*>(a.sync);
-  unsigned long long* ready = owner + 1;
+  unsigned long long* arrival = reinterpret_cast<unsigned long long*>(a.sync);
+  unsigned long long* ready = arrival + 1;
   int* tile_ctr = a.sync + 4;
-  const unsigned long long gid = grid_id() + 1;          // never 0, the initial contents
-  const unsigned long long tag = gid & ((1ull << (64 - kReadyShift)) - 1);
-  grid_dependency_wait();     // ids and state are final
-  if (t == 0) s_manager = atomicExch(owner, gid) != gid;
+  grid_dependency_wait();     // ids, state and the previous launch's words are final
+  if (t == 0) {
+    const unsigned long long v = atomicAdd(arrival, 1ull);
+    s_arrival = v;
+    if ((unsigned)(v & 0xffffffffu) == gridDim.x - 1)   // the last to arrive: next epoch
+      atomicExch(arrival, ((v >> 32) + 1) << 32);
+  }
   const ManageSmem sm = manage_smem(smem, a.m.E, a.m.S);
   const int my_id = (t < a.m.mk) ? a.m.ids[t] : -1;
   const bool staged = a.m.E <= kStepStageMaxExperts;
   long long step0 = 0;
-  if (staged) step0 = manage_stage<kStepThreads>(a.m, sm);   // overlaps the swap
+  if (staged) step0 = manage_stage<kStepThreads>(a.m, sm);   // overlaps the ticket
   __syncthreads();
+  // epoch + 1: the ready word's initial zero never matches
+  const unsigned long long tag = ((s_arrival >> 32) + 1) & ((1ull << (64 - kReadyShift)) - 1);
   int nm = 0;
-  if (s_manager) {
+  if ((s_arrival & 0xffffffffu) == 0) {
     manage_core<kStepThreads>(a.m, sm, my_id, staged, step0, &s_nm);
     if (t == 0) *tile_ctr = 0;          // this launch's tiles start at 0
     __syncthreads();                    // installs, miss list, n_miss and table complete
