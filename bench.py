@@ -55,8 +55,9 @@ L2_BYTES = 126 * 1024 * 1024
 # workload (S=64, 4 misses), from the ncu capture summarised in
 # profiles/step_kernel_s64_m4.txt.  The host-memory reads are not DRAM traffic and the
 # slot writes are still in L2 when the launch ends; printed with its source.
-STEP_DRAM_BYTES = None
-STEP_DRAM_SOURCE = "profiles/step_kernel_s64_m4.txt (ncu, one launch)"
+STEP_DRAM_BYTES = 52480
+STEP_DRAM_SOURCE = ("profiles/step_kernel_s64_m4.txt: ncu dram__bytes_read.sum + "
+                    "dram__bytes_write.sum of one launch (a capture, not this run)")
 # Layer-steps each worker of the reference arm times (K steps of R layer-steps).
 REF_LAYER_STEPS = 600
 

@@ -605,6 +605,10 @@ __device__ __forceinline__ unsigned long long load_acquire_gpu(const unsigned lo
   return v;
 }
 
+__device__ __forceinline__ void store_relaxed_gpu(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ void store_release_gpu(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -661,7 +665,15 @@ __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_cons
     if (t == 0) *tile_ctr = 0;          // this launch's tiles start at 0
     __syncthreads();                    // installs, miss list, n_miss and table complete
     nm = s_nm;
-    if (t == 0) store_release_gpu(ready, (tag << kReadyShift) | (unsigned long long)nm);
+    if (t == 0) {
+      const unsigned long long word = (tag << kReadyShift) | (unsigned long long)nm;
+      // Nothing to copy: the other CTAs only need the word itself, so it goes out without
+      // the release fence (which would first wait for this CTA's state stores).
+      if (nm == 0)
+        store_relaxed_gpu(ready, word);
+      else
+        store_release_gpu(ready, word);
+    }
     if (a.m.out_ids)
       remap_tail(a.m.ids, a.m.mk, a.m.E, a.m.out_ids, a.m.out_elem_bytes, sm.table, my_id,
                  kStepThreads);
@@ -680,7 +692,7 @@ __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_cons
         }
         if ((long long)(global_ns() - t0) > a.wait_ns) break;
         __nanosleep(ns);
-        if (ns < 256) ns <<= 1;
+        if (ns < 128) ns <<= 1;
       }
       if (got < 0) atomicAdd(a.sync + 5, 1);
       s_nm = got < 0 ? 0 : got;
