@@ -927,16 +927,21 @@ def decode_leg(a) -> dict:
     import bench_decode as bd
     import tempfile
     args = bd.parser().parse_args([
-        "--slots", str(a.decode_slots), "--gen", str(a.decode_gen),
+        "--slots", str(a.decode_slots), "--gen", str(a.decode_gen), "--reps", "3",
         "--routing", "model", "sticky-zipf", "--budget-s", str(a.decode_budget_s),
-        "--mode-timeout", "600", "--logdir",
+        "--mode-timeout", "600", "--control", "--logdir",
         str(Path(tempfile.gettempdir()) / "expert_cache_bench_decode")])
-    modes = [m for m in bd.plan_modes(args) if m["name"] != "offload-churn"]
+    # the second resident engine goes last, so the two resident runs bracket the others
+    planned = bd.plan_modes(args)
+    modes = [m for m in planned if m["name"] not in ("offload-churn", "resident-again",
+                                                     "resident-again-churn")]
+    modes.append(next(m for m in planned if m["name"] == "resident-again"))
     got = bd.run_suite(args, modes, echo=False)
     by = {r["mode"]: r for r in got["results"]}
     S = a.decode_slots
     res, cached, off = by.get("resident"), by.get(f"slots{S}"), by.get("offload")
     res_c, cached_c = by.get("resident-churn"), by.get(f"slots{S}-churn")
+    again = by.get("resident-again")
     out = {"workload": DECODE_WORKLOAD.format(gen=a.decode_gen), "slots": S,
            "experts": 128, "policy": args.policy,
            "resident_tok_s": res and res["decode_tok_s"],
@@ -944,6 +949,9 @@ def decode_leg(a) -> dict:
            "frac_of_resident": cached and cached["frac_of_resident"],
            "offload_uncached_tok_s": off and off["decode_tok_s"],
            "offload_uncached_frac_of_resident": off and off["frac_of_resident"],
+           "resident_again_tok_s": again and again["decode_tok_s"],
+           "resident_spread": (again and res and
+                               round(abs(again["decode_tok_s"] / res["decode_tok_s"] - 1), 4)),
            "cached": _decode_view(cached), "offload_uncached": _decode_view(off),
            "churn": {"routing": "every layer replays its own sticky-Zipf trace (config-1 "
                                 "locality: p_keep 0.7, Zipf(1.1)), both modes",
@@ -951,6 +959,9 @@ def decode_leg(a) -> dict:
                      "cached_tok_s": cached_c and cached_c["decode_tok_s"],
                      "frac_of_resident": cached_c and cached_c["frac_of_resident"],
                      "cached": _decode_view(cached_c)},
+           "timing": "engine clock, first to last token of a 128-token greedy generation, "
+                     "best of 3; resident_spread = |resident again / resident - 1|, the "
+                     "engine's own run-to-run spread on this host",
            "parity": "greedy tokens of each mode against its resident run; logprob "
                      "difference of the chosen tokens before any divergence",
            "all_within_1e-2_before_divergence":
