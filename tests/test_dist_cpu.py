@@ -25,7 +25,8 @@ d.init("gloo")
 d.barrier()
 m = d.max(float(d.rank + 1))
 s = d.sum(10.0)
-assert m == d.world == 2 and s == 20.0, (m, s)
+lo = d.min(float(d.rank + 1))
+assert m == d.world == 2 and s == 20.0 and lo == 1.0, (m, s, lo)
 d.barrier()
 print("RANK_OK", d.rank)
 d.close()
