@@ -281,8 +281,9 @@ EXPERT_CACHE_API int expert_cache_gather(void* d0, const void* s0, long b0, void
  *          sharing one must be ordered on one stream.
  *
  * Returns -1 on the rules of expert_cache_manage_remap and expert_cache_gather, when
- * S > EXPERT_CACHE_STEP_MAX_SLOTS, when sync is NULL or not 8-byte aligned, or when
- * max_wait_us < 0.
+ * S > EXPERT_CACHE_STEP_MAX_SLOTS, when sync is NULL or not 8-byte aligned, when
+ * max_wait_us < 0, or when max_inserts experts' slabs would be 2^31 or more 32 KiB tiles
+ * (64 GiB per expert at max_inserts = 1024).
  *
  * Replaces: the two launches of the reference's per-layer step (cache.py:118-161:
  * expert_cache_manage, kernels/expert_cache.hip:592-603, then expert_cache_gather,

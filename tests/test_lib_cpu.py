@@ -132,7 +132,8 @@ def step(h, E=8, S=4, mi=4, policy=0, mk=2, out=True, elem=4, sizes=(16,) * 6, p
 @pytest.mark.parametrize("kw", [dict(E=0), dict(S=0), dict(S=257), dict(mi=1025),
                                 dict(policy=2), dict(out=False), dict(elem=2),
                                 dict(sizes=(16,) * 5 + (24,)), dict(ptr=8), dict(chunks=0),
-                                dict(lanes=-1), dict(sync=0), dict(sync=514), dict(wait=-1)])
+                                dict(lanes=-1), dict(sync=0), dict(sync=514), dict(wait=-1),
+                                dict(sizes=(1 << 36,) * 6, mi=1024)])
 def test_step_refuses_bad_arguments(h, kw):
     # refused before any CUDA call: these return -1 on a machine without a GPU
     assert step(h, **kw) == -1

@@ -1097,6 +1097,9 @@ int expert_cache_step(const int* topk_ids, int mk, int E, int S, int max_distinc
   const long bytes[EXPERT_CACHE_GATHER_SLOTS] = {b0, b1, b2, b3, b4, b5};
   int rc = make_gather_args(dsts, srcs, bytes, miss, n_miss, &a.g);
   if (rc != 0) return rc;
+  // the launch's tile counter is 32-bit: every tile index of the largest miss list fits
+  if ((long long)a.g.tile_start[a.g.nbuf] * (max_inserts > 0 ? max_inserts : 1) >= INT_MAX)
+    return -1;
   if (chunks <= 0 || lanes <= 0) return -1;
   a.chunks = chunks;
   a.lanes = lanes;
