@@ -573,7 +573,8 @@ __global__ void __launch_bounds__(kGatherThreads)
 //   - copy: every CTA claims 32 KiB tiles of the miss list's copy from the tile counter
 //     until none are left.  The policy CTA claims tiles too, so it alone completes the
 //     copy if no other CTA ever sees the word: a wait that runs out (counted, never
-//     silent) costs time, never bytes.
+//     silent) costs time, never bytes.  For the same reason a helper whose staged table
+//     already holds every routed expert leaves without waiting.
 // While thread 0 takes its ticket, every thread already stages the state into shared
 // memory (small E only), so the ticket's round trip overlaps the state load.
 //
@@ -680,6 +681,19 @@ __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_cons
     // running install count: only the policy CTA writes it, launches are stream-ordered
     if (t == 0) *reinterpret_cast<long long*>(a.sync + 6) += nm;
   } else {
+    if (staged) {
+      // A helper that sees every routed expert already in a slot leaves at once.  Its view
+      // may be the table before or after the policy CTA's installs, or a mix of the two;
+      // either way leaving only forgoes helping: the policy CTA claims whatever tiles
+      // are left.  A step that installs nothing never changes the table, so every helper
+      // of such a step sees it exactly and none of them waits.
+      bool missing = my_id >= 0 && my_id < a.m.E && sm.table[my_id] < 0;
+      for (int i = t + kStepThreads; i < a.m.mk; i += kStepThreads) {
+        const int e = a.m.ids[i];
+        missing |= e >= 0 && e < a.m.E && sm.table[e] < 0;
+      }
+      if (!__syncthreads_or(missing)) return;
+    }
     if (t == 0) {
       const unsigned long long t0 = global_ns();
       unsigned ns = 32;
