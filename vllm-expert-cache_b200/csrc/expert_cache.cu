@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_cons
   int nm = 0;
   if ((s_arrival & 0xffffffffu) == 0) {
     manage_core<kStepThreads>(a.m, sm, my_id, staged, step0, &s_nm);
-    if (t == 0) *tile_ctr = 0;          // this launch's tiles start at 0
+    if (t == 0 && s_nm > 0) *tile_ctr = 0;   // this launch's tiles start at 0
     __syncthreads();                    // installs, miss list, n_miss and table complete
     nm = s_nm;
     if (t == 0) {
@@ -678,8 +678,10 @@ __global__ void __launch_bounds__(kStepThreads, 2) step_kernel(const __grid_cons
     if (a.m.out_ids)
       remap_tail(a.m.ids, a.m.mk, a.m.E, a.m.out_ids, a.m.out_elem_bytes, sm.table, my_id,
                  kStepThreads);
-    // running install count: only the policy CTA writes it, launches are stream-ordered
-    if (t == 0) *reinterpret_cast<long long*>(a.sync + 6) += nm;
+    // running install count: only the policy CTA writes it, launches are stream-ordered;
+    // a step without installs skips the read-modify-write (a memory round trip at the end
+    // of the launch)
+    if (t == 0 && nm > 0) *reinterpret_cast<long long*>(a.sync + 6) += nm;
   } else {
     if (staged) {
       // A helper that sees every routed expert already in a slot leaves at once.  Its view
