@@ -61,3 +61,42 @@ def test_plan_and_compare():
     assert r["first_divergent_token"] == 2
     assert abs(r["max_abs_logprob_diff"] - 0.0005) < 1e-9   # only positions before it
     assert r["resident_top2_gap_at_divergence"] == 0.0156
+
+
+def test_bench_decode_object(monkeypatch):
+    """bench.py's decode object from a stubbed suite: the cached fraction is taken against
+    the faster resident engine, the spread between the two is reported beside it."""
+    import bench
+
+    def result(mode, tps, frac, installs=None):
+        cache = None if installs is None else {"timed_installs_per_layer_step": installs,
+                                               "installs_per_layer_step": installs,
+                                               "layer_steps": 10, "installs": 1,
+                                               "armed_layers": 48, "step_wait_timeouts": 0}
+        return {"mode": mode, "decode_tok_s": tps, "frac_of_resident": frac,
+                "tokens_match_resident": True, "max_abs_logprob_diff": 0.0,
+                "first_divergent_token": None, "resident_top2_gap_at_divergence": None,
+                "cache": cache}
+
+    modes_seen = []
+
+    def fake_suite(args, modes, echo=True):
+        modes_seen.extend(m["name"] for m in modes)
+        res = [result("resident", 250.0, 1.0), result("offload", 25.0, 0.1),
+               result("slots64", 240.0, 0.96, 0.0), result("resident-churn", 240.0, 1.0),
+               result("slots64-churn", 150.0, 0.625, 0.44),
+               result("resident-again", 300.0, 1.2)]
+        return {"results": res, "ok": True,
+                "summary": {"all_within_1e-2_before_divergence": True, "skipped": [],
+                            "failed": {}, "wall_s": 1.0}}
+
+    monkeypatch.setattr(bd, "run_suite", fake_suite)
+    a = bench.parse(["--decode-slots", "64"])
+    out = bench.decode_leg(a)
+    assert modes_seen == ["resident", "offload", "slots64", "resident-churn",
+                          "slots64-churn", "resident-again"]
+    assert out["frac_of_resident"] == 0.8            # 240 / max(250, 300)
+    assert out["frac_of_first_resident"] == 0.96
+    assert out["resident_spread"] == 0.2
+    assert out["churn"]["frac_of_resident"] == 0.625
+    assert out["cached"]["timed_installs_per_layer_step"] == 0.0
