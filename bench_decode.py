@@ -583,6 +583,10 @@ def parser() -> argparse.ArgumentParser:
     ap.add_argument("--reps", type=int, default=2, help="timed generations per length; the "
                     "best is kept")
     ap.add_argument("--mode-timeout", type=int, default=1200)
+    ap.add_argument("--repeat", type=int, default=1,
+                    help="run the whole mode list this many times, interleaved (resident, "
+                         "cached, resident, cached, ...), and report each mode's mean and "
+                         "spread: engines of one configuration differ by several percent")
     ap.add_argument("--budget-s", type=float, default=0,
                     help="stop starting new modes once this much wall time has passed "
                          "(0 = no limit); skipped modes are listed in the summary")
@@ -651,6 +655,8 @@ def run_suite(a, modes=None, echo=True) -> dict:
     write_model_dir(model_dir, a.layers, a.prompt + a.gen + 16, a.quant, a.arch)
     write_plugin_site(site)
     modes = plan_modes(a) if modes is None else modes
+    if a.repeat > 1:
+        modes = [dict(m, name=f"{m['name']}#{i}") for i in range(a.repeat) for m in modes]
     t0 = time.time()
     results, skipped, failed = [], [], {}
     bases: dict[str, dict] = {}
@@ -681,7 +687,22 @@ def run_suite(a, modes=None, echo=True) -> dict:
     # two runs share (before any divergence); divergences are reported with the resident
     # run's own top-1/top-2 margin at that position
     ok = all(r["max_abs_logprob_diff"] <= 1e-2 for r in results) and not failed
+    repeated = {}
+    if a.repeat > 1:
+        for r in results:
+            repeated.setdefault(r["mode"].split("#")[0], []).append(r["decode_tok_s"])
+        base_mean = None
+        for name, v in repeated.items():
+            mean = sum(v) / len(v)
+            repeated[name] = {"mean_tok_s": round(mean, 2), "min": min(v), "max": max(v),
+                              "runs": v}
+            if base_mean is None and name.startswith("resident"):
+                base_mean = mean
+        for name, v in repeated.items():
+            if base_mean:
+                v["mean_frac_of_resident"] = round(v["mean_tok_s"] / base_mean, 4)
     summary = {"summary": "decode", "all_within_1e-2_before_divergence": ok,
+               "repeated": repeated,
                "tokens_identical": {r["mode"]: r["tokens_match_resident"] for r in results},
                "decode_tok_s": {r["mode"]: r["decode_tok_s"] for r in results},
                "frac_of_resident": {r["mode"]: r["frac_of_resident"] for r in results},

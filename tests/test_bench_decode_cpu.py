@@ -100,3 +100,24 @@ def test_bench_decode_object(monkeypatch):
     assert out["resident_spread"] == 0.2
     assert out["churn"]["frac_of_resident"] == 0.625
     assert out["cached"]["timed_installs_per_layer_step"] == 0.0
+
+
+def test_repeat_interleaves_and_averages(monkeypatch, tmp_path):
+    rates = iter([250.0, 240.0, 270.0, 250.0, 260.0, 245.0])   # R, C, R, C, R, C
+    order = []
+
+    def fake_run_mode(mode, args, model_dir, site, logdir):
+        order.append(mode["name"])
+        return {"mode": mode["name"], "decode_tok_s": next(rates), "tokens": [1, 2],
+                "logprobs": [-0.1, -0.1], "gaps": [1.0, 1.0], "cache": None}
+
+    monkeypatch.setattr(bd, "run_mode", fake_run_mode)
+    a = bd.parser().parse_args(["--slots", "64", "--no-offload-baseline", "--repeat", "3",
+                                "--logdir", str(tmp_path)])
+    got = bd.run_suite(a, echo=False)
+    assert order == ["resident#0", "slots64#0", "resident#1", "slots64#1", "resident#2",
+                     "slots64#2"]
+    rep = got["summary"]["repeated"]
+    assert rep["resident"]["mean_tok_s"] == 260.0 and rep["slots64"]["mean_tok_s"] == 245.0
+    assert rep["slots64"]["mean_frac_of_resident"] == round(245.0 / 260.0, 4)
+    assert rep["slots64"]["min"] == 240.0 and rep["slots64"]["max"] == 250.0
